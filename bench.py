@@ -1,0 +1,506 @@
+#!/usr/bin/env python3
+"""Benchmark: post-prefill KV-cache compression on B200, sharded by layer.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 4]
+
+Workload (default): BASELINE config 4 -- Llama-3-70B-shaped 128K cache, 80 layers
+x 8 KV heads x head_dim 128, batch 1, T=131072, fp16 (42.95 GB of K+V), RoPE base
+5e5, 'max' preset: K2V2 + 80 % eviction with the key-key scorer on layer 0,
+first/last 2 layers protected at fp16.  Synthetic data (seeded N(0,1) keys with
+outlier channels + RoPE, N(0,1) values), generated on the device.
+
+One step = score layer 0 (each rank scores its share of the heads; per-head
+column sums are all-gathered over NCCL) -> keep set -> compress every layer the
+rank owns (one launch) + fp16 gather of its protected layers -> all-gather of
+per-layer compressed sizes.  Layers are assigned to ranks by cost (strong
+scaling: the cache is fixed, N GPUs share it).  value = fp16-in bytes of the
+whole cache / max-over-ranks step time.  Inputs (42.95 GB) are far larger than
+L2, so no flush is needed between steps.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import sys
+import threading
+import time
+
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from nexusquant_b200 import kernels as K  # noqa: E402
+from nexusquant_b200 import synthetic as syn  # noqa: E402
+from nexusquant_b200.pipeline import kept_capacity, n_keep_for  # noqa: E402
+
+METRIC = "KV compress GB/s (fp16 in) & dequant GB/s, % of HBM peak, at 1/2/4/8 B200"
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# ------------------------------------------------------------------ clocks (NVML)
+class ClockSampler:
+    """Samples SM clock and clock-event reasons every ~5 ms on a background thread."""
+
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+               0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+               0x100: "display_clock_setting"}
+
+    def __init__(self, index: int):
+        self.ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self.max_mhz = None
+        self.samples, self.reasons = [], 0
+        self._stop = threading.Event()
+
+    def _run(self):
+        while not self._stop.is_set():
+            self.sample()
+            time.sleep(0.005)
+
+    def sample(self):
+        if not self.ok:
+            return
+        try:
+            self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+            self.reasons |= self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+        except Exception:
+            pass
+
+    def __enter__(self):
+        self.sample()
+        self.t = threading.Thread(target=self._run, daemon=True)
+        self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        self.t.join()
+        self.sample()
+
+    def report(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["nvml unavailable"]}
+        s = sorted(self.samples)
+        return {"sm_mhz": s[len(s) // 2], "sm_max_mhz": self.max_mhz, "samples": len(s),
+                "reasons": [n for b, n in self.REASONS.items() if self.reasons & b]}
+
+
+# -------------------------------------------------------------------------- plan
+def assign_layers(n_layers: int, protected: set, world: int):
+    """Cost-balanced layer -> rank assignment (protected layers cost ~1.6x a quantized one:
+    they move 2 x 2 x d bytes per kept row instead of 2 x d + packed bytes)."""
+    cost = {l: (1.6 if l in protected else 1.0) for l in range(n_layers)}
+    order = sorted(range(n_layers), key=lambda l: (-cost[l], l))
+    load = [0.0] * world
+    owned = [[] for _ in range(world)]
+    for l in order:
+        r = min(range(world), key=lambda i: (load[i], i))
+        owned[r].append(l)
+        load[r] += cost[l]
+    return [sorted(o) for o in owned]
+
+
+class Shard:
+    """One rank's part of the compression of a config-4-shaped cache."""
+
+    def __init__(self, cfg, rank: int, world: int, device, group=None):
+        self.cfg, self.rank, self.world, self.dev, self.group = cfg, rank, world, device, group
+        L = cfg.n_layers
+        pb = cfg.protect_boundary
+        self.protected = set(range(pb)) | set(range(L - pb, L)) if pb else set()
+        self.owned = assign_layers(L, self.protected, world)[rank]
+        self.quant = [l for l in self.owned if l not in self.protected]
+        self.prot = [l for l in self.owned if l in self.protected]
+        h = cfg.heads
+        per = math.ceil(h / world)
+        self.h0, self.h1 = min(h, rank * per), min(h, (rank + 1) * per)
+        self.per = per
+        self.nk = n_keep_for(cfg.seq, cfg.sliding_window, cfg.eviction_rate)
+        self.cap = kept_capacity(cfg.seq, cfg.sliding_window, self.nk)
+        # resident data: this rank's layers, plus layer 0's keys for scoring
+        self.K, self.V = {}, {}
+        for l in self.owned:
+            self.K[l], self.V[l] = syn.device_layer(cfg, l, device)
+        self.K0 = self.K[0] if 0 in self.K else syn.device_layer(cfg, 0, device)[0]
+        b, _, T, d = self.K0.shape
+        dp = K.next_pow2(d)
+        self.levels = (2 ** cfg.key_bits, 2 ** cfg.value_bits)
+        n = self.cap
+        self.codes = [K.LayerCodes(
+            torch.empty((b, h, n, K.packed_bytes(dp, self.levels[0])), dtype=torch.uint8, device=device),
+            torch.empty((b, h, n, K.packed_bytes(dp, self.levels[1])), dtype=torch.uint8, device=device),
+            torch.empty((b, h, n), dtype=torch.float16, device=device),
+            torch.empty((b, h, n), dtype=torch.float16, device=device), *self.levels) for _ in self.quant]
+        self.prot_out = {l: (torch.empty((b, h, n, d), dtype=torch.float16, device=device),
+                             torch.empty((b, h, n, d), dtype=torch.float16, device=device)) for l in self.prot}
+        self.gathered = torch.empty((world * b * per, T), dtype=torch.float32, device=device)
+        sizes = [0] * L
+        for l in self.quant:
+            sizes[l] = b * h * n * (K.packed_bytes(dp, self.levels[0]) + K.packed_bytes(dp, self.levels[1]) + 4)
+        for l in self.prot:
+            sizes[l] = 2 * b * h * n * d * 2
+        self.sizes = torch.tensor(sizes, dtype=torch.int64, device=device)
+        self.sizes_all = torch.zeros((world, L), dtype=torch.int64, device=device)
+        self.launches = 0
+
+    # bytes
+    def fp16_in_bytes_total(self) -> int:
+        return self.cfg.fp16_bytes
+
+    def compress_algo_bytes(self) -> int:
+        """Algorithmic bytes of this rank's compress launch: read 2*d bytes per kept K and V
+        row, write packed codes + fp16 scale per row, read the kept index per (row, head) once."""
+        b, h, d = self.cfg.batch, self.cfg.heads, self.cfg.head_dim
+        dp = K.next_pow2(d)
+        pk, pv = K.packed_bytes(dp, self.levels[0]), K.packed_bytes(dp, self.levels[1])
+        rows = len(self.quant) * b * h * self.cap
+        return rows * (2 * d * 2 + pk + pv + 4)
+
+    def step(self):
+        cfg = self.cfg
+        b, h, T = cfg.batch, cfg.heads, cfg.seq
+        if self.h1 > self.h0:
+            ph = K.score_keykey(self.K0, 32, head_range=(self.h0, self.h1), per_head=True)
+            self.launches += 3
+        else:
+            ph = torch.zeros((b, 0, T), dtype=torch.float32, device=self.dev)
+        if self.world > 1:
+            buf = torch.zeros((b, self.per, T), dtype=torch.float32, device=self.dev)
+            buf[:, :ph.shape[1]] = ph
+            dist.all_gather_into_tensor(self.gathered, buf.reshape(b * self.per, T), group=self.group)
+            allh = self.gathered.reshape(self.world, b, self.per, T).transpose(0, 1).reshape(b, -1, T)[:, :h]
+        else:
+            allh = ph
+        imp = K.reduce_heads(allh, float(h))
+        idx, cnt = K.select_keep(imp, cfg.sliding_window, self.nk)
+        self.launches += 2
+        if self.quant:
+            K.compress_layers([self.K[l] for l in self.quant], [self.V[l] for l in self.quant],
+                              key_levels=self.levels[0], value_levels=self.levels[1], kept_idx=idx[:, :self.cap],
+                              kept_count=cnt, n_kept=self.cap, rope_base=cfg.rope_base, rope_rows=T,
+                              codes_out=self.codes)
+            self.launches += math.ceil(len(self.quant) / 96)
+        for l in self.prot:
+            K.gather_rows(self.K[l], idx[:, :self.cap], self.cap, cnt, out=self.prot_out[l][0])
+            K.gather_rows(self.V[l], idx[:, :self.cap], self.cap, cnt, out=self.prot_out[l][1])
+            self.launches += 2
+        self.kept_idx, self.kept_count = idx, cnt
+        if self.world > 1:
+            # global index of the compressed cache: per-layer byte sizes from every rank
+            dist.all_gather_into_tensor(self.sizes_all, self.sizes, group=self.group)
+
+    def compress_only(self):
+        K.compress_layers([self.K[l] for l in self.quant], [self.V[l] for l in self.quant],
+                          key_levels=self.levels[0], value_levels=self.levels[1],
+                          kept_idx=self.kept_idx[:, :self.cap], kept_count=self.kept_count, n_kept=self.cap,
+                          rope_base=self.cfg.rope_base, rope_rows=self.cfg.seq, codes_out=self.codes)
+
+    def dequant(self, outs):
+        return K.decompress_layers(self.codes, self.kept_idx[:, :self.cap], head_dim=self.cfg.head_dim,
+                                   count=self.kept_count, rope_base=self.cfg.rope_base, out_k=outs[0],
+                                   out_v=outs[1])
+
+
+def timed(fn, steps, warmup, world, group=None):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier(group=group)
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(steps):
+        fn()
+    e1.record(s)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+        ms = float(t.item())
+        dist.barrier(group=group)
+    return ms
+
+
+# --------------------------------------------------------------------- CPU leg
+def cpu_sample(cfg, seconds_hint: float = 15.0):
+    """Time the oracle port on this host: score layer 0 (all heads, float64) + select +
+    compress of 2 quantized layers' kept rows; extrapolate to the whole cache.  Returns
+    (GB/s fp16-in, threads, description)."""
+    import numpy as np
+    from concurrent.futures import ThreadPoolExecutor
+
+    from oracle import oracle as orc
+    threads = os.cpu_count() or 1
+    orc.lib()
+    b, h, T, d = cfg.batch, cfg.heads, cfg.seq, cfg.head_dim
+    g = torch.Generator().manual_seed(7)
+    k0 = torch.randn(b, h, T, d, generator=g)
+    t0 = time.perf_counter()
+    obs = 32
+    scale = float(np.float32(d ** -0.5))
+    k0n = k0.numpy()
+
+    def one(hi):
+        return orc.attn_colsum(k0n[0, hi, T - obs:], k0n[0, hi], scale)
+    with ThreadPoolExecutor(threads) as ex:
+        cols = list(ex.map(one, range(h)))
+    imp = (np.sum(cols, 0) / h)[None]
+    m = orc.keep_mask(imp, T, cfg.sliding_window, cfg.eviction_rate)
+    t_score = time.perf_counter() - t0
+    kept = np.nonzero(m[0])[0]
+    n = len(kept)
+    cos, sin = orc.rope_tables(kept, d, cfg.rope_base)
+    cr, sr = np.tile(cos, (h, 1)), np.tile(sin, (h, 1))
+    rows = torch.randn(2, h * n, d, generator=g).numpy()
+    t1 = time.perf_counter()
+    for _ in range(2):
+        kc, ks = orc.quantize(rows[0], K.next_pow2(d), 2 ** cfg.key_bits, cr, sr)
+        vc, vs = orc.quantize(rows[1], K.next_pow2(d), 2 ** cfg.value_bits)
+        orc.pack(kc, 2 ** cfg.key_bits)
+        orc.pack(vc, 2 ** cfg.value_bits)
+    t_layer = (time.perf_counter() - t1) / 2
+    n_q = cfg.n_layers - 2 * cfg.protect_boundary
+    total = t_score + n_q * t_layer
+    gbs = cfg.fp16_bytes / total / 1e9
+    desc = (f"oracle port (C, OpenMP {threads} threads): key-key score of layer 0 ({h} heads x {T} tokens, "
+            f"float64) + keep set, measured {t_score:.2f}s; compress of 2 quantized layers' kept rows "
+            f"({n} tokens x {h} heads, K+V) measured {t_layer:.3f}s/layer; extrapolated to {n_q} quantized "
+            f"layers (protected-layer copies not counted)")
+    return gbs, threads, desc
+
+
+# ------------------------------------------------------------------------ e2e
+def e2e_leg(sh: Shard, steps: int):
+    """End to end through the public kernels from pinned host memory: each step copies the
+    rank's layers host->device (copy stream, overlapped with compression of earlier layers)
+    and copies the compressed outputs device->host."""
+    cfg = sh.cfg
+    dev = sh.dev
+    try:
+        host = {l: (torch.empty(sh.K[l].shape, dtype=sh.K[l].dtype, pin_memory=True),
+                    torch.empty(sh.V[l].shape, dtype=sh.V[l].dtype, pin_memory=True)) for l in sh.owned}
+        host_k0 = None if 0 in sh.K else torch.empty(sh.K0.shape, dtype=sh.K0.dtype, pin_memory=True)
+    except RuntimeError as e:
+        return None, f"pinned host allocation failed: {e}"
+    for l in sh.owned:
+        host[l][0].copy_(sh.K[l])
+        host[l][1].copy_(sh.V[l])
+    if host_k0 is not None:
+        host_k0.copy_(sh.K0)
+    out_host = [(torch.empty(c.k_codes.shape, dtype=torch.uint8, pin_memory=True),
+                 torch.empty(c.v_codes.shape, dtype=torch.uint8, pin_memory=True),
+                 torch.empty(c.k_scales.shape, dtype=torch.float16, pin_memory=True),
+                 torch.empty(c.v_scales.shape, dtype=torch.float16, pin_memory=True)) for c in sh.codes]
+    prot_host = {l: (torch.empty(sh.prot_out[l][0].shape, dtype=torch.float16, pin_memory=True),
+                     torch.empty(sh.prot_out[l][1].shape, dtype=torch.float16, pin_memory=True))
+                 for l in sh.prot}
+    cp = torch.cuda.Stream(dev)
+    dn = torch.cuda.Stream(dev)
+    comp = torch.cuda.current_stream(dev)
+    h2d = sum(host[l][0].numel() * host[l][0].element_size() * 2 for l in sh.owned)
+    if host_k0 is not None:
+        h2d += host_k0.numel() * host_k0.element_size()
+    d2h = sum(sum(t.numel() * t.element_size() for t in o) for o in out_host)
+    d2h += sum(t.numel() * t.element_size() * 2 for t, _ in prot_host.values())
+
+    def step():
+        ev = {}
+        with torch.cuda.stream(cp):
+            if host_k0 is not None:
+                sh.K0.copy_(host_k0, non_blocking=True)
+            order = ([0] if 0 in sh.owned else []) + [l for l in sh.owned if l != 0]
+            for l in order:
+                sh.K[l].copy_(host[l][0], non_blocking=True)
+                sh.V[l].copy_(host[l][1], non_blocking=True)
+                e = torch.cuda.Event()
+                e.record(cp)
+                ev[l] = e
+        first = ev[order[0]] if order else None
+        if host_k0 is not None:
+            e0 = torch.cuda.Event()
+            e0.record(cp)
+            comp.wait_event(e0)
+        elif first is not None:
+            comp.wait_event(first)
+        # keep set from layer 0, then compress layers as they arrive
+        b, h, T = cfg.batch, cfg.heads, cfg.seq
+        ph = K.score_keykey(sh.K0, 32, head_range=(sh.h0, sh.h1), per_head=True) if sh.h1 > sh.h0 else \
+            torch.zeros((b, 0, T), dtype=torch.float32, device=dev)
+        if sh.world > 1:
+            buf = torch.zeros((b, sh.per, T), dtype=torch.float32, device=dev)
+            buf[:, :ph.shape[1]] = ph
+            dist.all_gather_into_tensor(sh.gathered, buf.reshape(b * sh.per, T))
+            ph = sh.gathered.reshape(sh.world, b, sh.per, T).transpose(0, 1).reshape(b, -1, T)[:, :h]
+        imp = K.reduce_heads(ph, float(h))
+        idx, cnt = K.select_keep(imp, cfg.sliding_window, sh.nk)
+        done = torch.cuda.Event()
+        for i, l in enumerate(sh.quant):
+            comp.wait_event(ev[l])
+            K.compress_layers([sh.K[l]], [sh.V[l]], key_levels=sh.levels[0], value_levels=sh.levels[1],
+                              kept_idx=idx[:, :sh.cap], kept_count=cnt, n_kept=sh.cap, rope_base=cfg.rope_base,
+                              rope_rows=T, codes_out=[sh.codes[i]])
+            e = torch.cuda.Event()
+            e.record(comp)
+            dn.wait_event(e)
+            with torch.cuda.stream(dn):
+                c = sh.codes[i]
+                for src, dst in zip((c.k_codes, c.v_codes, c.k_scales, c.v_scales), out_host[i]):
+                    dst.copy_(src, non_blocking=True)
+        for l in sh.prot:
+            comp.wait_event(ev[l])
+            K.gather_rows(sh.K[l], idx[:, :sh.cap], sh.cap, cnt, out=sh.prot_out[l][0])
+            K.gather_rows(sh.V[l], idx[:, :sh.cap], sh.cap, cnt, out=sh.prot_out[l][1])
+            e = torch.cuda.Event()
+            e.record(comp)
+            dn.wait_event(e)
+            with torch.cuda.stream(dn):
+                prot_host[l][0].copy_(sh.prot_out[l][0], non_blocking=True)
+                prot_host[l][1].copy_(sh.prot_out[l][1], non_blocking=True)
+        done.record(dn)
+        comp.wait_event(done)
+
+    step()
+    torch.cuda.synchronize()
+    ms = timed(step, steps, 1, sh.world, sh.group)
+    return {"value": round(cfg.fp16_bytes * steps / (ms / 1e3) / 1e9, 3), "unit": "GB/s",
+            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+            "steps": steps, "ms_per_step": round(ms / steps, 3)}, None
+
+
+# ------------------------------------------------------------------- reference
+def run_reference(args, cfg, rank, world):
+    if rank != 0:
+        return
+    vals = []
+    for i in range(args.warmup + args.steps):
+        gbs, threads, desc = cpu_sample(cfg)
+        if i >= args.warmup:
+            vals.append(gbs)
+    v = sum(vals) / len(vals)
+    line = {"metric": METRIC, "impl": "reference", "value": round(v, 4), "unit": "GB/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": cfg.name, "layers": cfg.n_layers, "batch": cfg.batch, "heads": cfg.heads,
+                       "seq": cfg.seq, "head_dim": cfg.head_dim},
+            "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+                             "sample": desc},
+            "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------ main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", type=int, default=4)
+    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--profile", action="store_true", help="a few steps only (for ncu launch lists)")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    cfg = syn.CONFIGS[args.config]
+    if args.impl == "reference":
+        run_reference(args, cfg, rank, world)
+        return
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    group = None
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    sh = Shard(cfg, rank, world, dev, group)
+    torch.cuda.synchronize()
+
+    clocks = ClockSampler(local)
+    sh.step()  # first call builds the RoPE table cache
+    torch.cuda.synchronize()
+    sh.launches = 0
+    with clocks:
+        ms = timed(sh.step, args.steps, args.warmup, world, group)
+    launches = sh.launches * args.steps // (args.steps + args.warmup)
+
+    # kernel-only: the compress launch on its stream, and the dequantize launch
+    kms = timed(sh.compress_only, args.steps, 2, 1) / args.steps
+    outs = ([torch.empty((cfg.batch, cfg.heads, sh.cap, cfg.head_dim), dtype=torch.float16, device=dev)
+             for _ in sh.quant],
+            [torch.empty((cfg.batch, cfg.heads, sh.cap, cfg.head_dim), dtype=torch.float16, device=dev)
+             for _ in sh.quant])
+    dms = timed(lambda: sh.dequant(outs), args.steps, 2, 1) / args.steps if sh.quant else float("nan")
+    peak, peak_kind = peaks()
+    algo = sh.compress_algo_bytes()
+    achieved = algo / (kms / 1e3) / 1e9 if sh.quant else 0.0
+    dq_bytes = algo  # dequantize moves the same bytes in the other direction
+    dq_achieved = dq_bytes / (dms / 1e3) / 1e9 if sh.quant else 0.0
+    traffic = None
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            traffic = json.load(f).get(cfg.name, {}).get(f"compress_world{world}")
+    except Exception:
+        pass
+
+    e2e, e2e_err = (None, "disabled")
+    if not args.no_e2e and not args.profile:
+        e2e, e2e_err = e2e_leg(sh, args.e2e_steps)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu and not args.profile:
+        gbs, threads, desc = cpu_sample(cfg)
+        cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port", "sample": desc}
+
+    value = cfg.fp16_bytes * args.steps / (ms / 1e3) / 1e9
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": cfg.name, "layers": cfg.n_layers, "batch": cfg.batch, "heads": cfg.heads,
+                       "seq": cfg.seq, "head_dim": cfg.head_dim, "key_bits": cfg.key_bits,
+                       "value_bits": cfg.value_bits, "eviction_rate": cfg.eviction_rate,
+                       "kept_tokens": sh.cap, "protected_layers": sorted(sh.protected),
+                       "parallelism": f"layer-sharded x{world}", "l2": "inputs (42.95 GB) larger than L2; no flush"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
+                         "kernel": "compress_kernel", "launch_ms": round(kms, 4), "algo_bytes": algo},
+            "dequant": {"value": round(dq_achieved, 1), "unit": "GB/s", "frac": round(dq_achieved / peak, 4),
+                        "launch_ms": round(dms, 4), "algo_bytes": dq_bytes},
+            "cpu_baseline": cpu,
+            "e2e": e2e if e2e is not None else {"value": None, "unit": "GB/s", "error": e2e_err},
+            "gpu_launches": launches,
+            "clocks": clocks.report(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
