@@ -149,8 +149,8 @@ def test_compress_decompress_roundtrip_vs_oracle(orc, d, lk):
     v16 = lc.v_scales.cpu().numpy().reshape(-1).astype(np.float32)
     kr = orc.dequantize(o["k_codes"], k16, d, o["cos"], o["sin"]).astype(np.float16)
     vr = orc.dequantize(o["v_codes"], v16, d).astype(np.float16)
-    assert np.array_equal(ok.cpu().numpy().reshape(-1, d), kr)
-    assert np.array_equal(ov.cpu().numpy().reshape(-1, d), vr)
+    assert np.array_equal(ok[0].cpu().numpy().reshape(-1, d), kr)
+    assert np.array_equal(ov[0].cpu().numpy().reshape(-1, d), vr)
 
 
 def test_kept_count_ragged_rows(orc):
