@@ -45,7 +45,8 @@ enum {
   NQ_ERR_CUDA = -3,          /* a CUDA launch or query failed */
   NQ_ERR_TIMEOUT = -4,       /* a bounded device-side wait expired */
   NQ_ERR_WORKSPACE = -5,     /* workspace missing or smaller than *_workspace_size() */
-  NQ_ERR_ALIGNMENT = -6      /* a pointer or stride breaks the 16-byte alignment rule */
+  NQ_ERR_ALIGNMENT = -6,     /* a pointer or stride breaks the 16-byte alignment rule */
+  NQ_ERR_TOO_LARGE = -7      /* problem needs more than the library's built-in scratch */
 };
 
 typedef enum { NQ_F16 = 0, NQ_BF16 = 1, NQ_F32 = 2 } nq_dtype_t;
@@ -183,6 +184,27 @@ nq_status_t nq_score_attention(const void *q, const void *k, int32_t in_dtype, i
                                int64_t k_stride_t, int32_t q_pos0, int32_t accumulate, float *importance,
                                void *workspace, size_t workspace_bytes, nq_stream_t stream);
 size_t nq_score_attention_workspace_size(int32_t batch, int32_t q_heads, int32_t n_q, int32_t seq);
+
+/*
+ * nq_score_keykey without any scratch from the caller or from cudaMalloc.
+ * No counterpart in the reference.  For callers that cannot allocate device
+ * memory when they score (inside an allocator or memory pool that must not be
+ * re-entered, engines that pre-reserve all device memory, bindings without a
+ * cudaMalloc): the scratch is a fixed array inside this library, of
+ * NQ_NOALLOC_SCRATCH_BYTES per GPU, held from load until exit.  Same arguments
+ * and results as nq_score_keykey minus the workspace.  Returns NQ_ERR_TOO_LARGE
+ * when the problem needs more scratch than that: roughly
+ * batch * (head_end - head_begin) * seq * (4 + 8 * min(obs_window, seq) / 128)
+ * bytes (without the first term when per_head = 1); 8 MiB covers one 128K-token,
+ * 8-head layer.  The first call on a device looks up the array's address with
+ * that device current; make it before any stream capture.  All calls on a device
+ * share the array: calls that overlap on the GPU race and must be serialised.
+ */
+#define NQ_NOALLOC_SCRATCH_BYTES (8u << 20)
+nq_status_t nq_score_keykey_noalloc(const void *k, int32_t in_dtype, int32_t batch, int32_t heads, int32_t seq,
+                                    int32_t head_dim, int64_t stride_b, int64_t stride_h, int64_t stride_t,
+                                    int32_t obs_window, int32_t head_begin, int32_t head_end, int32_t per_head,
+                                    float *out, nq_stream_t stream);
 
 /*
  * out[b, t] (=, or += when accumulate) (sum over h = 0 .. heads-1, in order, of

@@ -24,7 +24,7 @@ NQ_OK = 0
 _STATUS = {
     0: "ok", -1: "invalid argument", -2: "unsupported shape or dtype", -3: "CUDA error",
     -4: "device-side wait timed out", -5: "workspace missing or too small",
-    -6: "pointer or stride not 16-byte aligned",
+    -6: "pointer or stride not 16-byte aligned", -7: "problem exceeds the library's built-in scratch size",
 }
 
 
@@ -75,6 +75,8 @@ _PROTOS = {
     "nq_score_keykey": (c_i32, [c_vp, c_i32, c_i32, c_i32, c_i32, c_i32, c_i64, c_i64, c_i64, c_i32, c_i32,
                                 c_i32, c_i32, c_vp, c_vp, c_size, c_vp]),
     "nq_score_keykey_workspace_size": (c_size, [c_i32, c_i32, c_i32, c_i32]),
+    "nq_score_keykey_noalloc": (c_i32, [c_vp, c_i32, c_i32, c_i32, c_i32, c_i32, c_i64, c_i64, c_i64, c_i32, c_i32,
+                                        c_i32, c_i32, c_vp, c_vp]),
     "nq_score_attention": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_i64, c_i64,
                                    c_i64, c_i64, c_i64, c_i64, c_i32, c_i32, c_vp, c_vp, c_size, c_vp]),
     "nq_score_attention_workspace_size": (c_size, [c_i32, c_i32, c_i32, c_i32]),

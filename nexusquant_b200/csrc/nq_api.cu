@@ -37,6 +37,7 @@ const char* nq_status_string(nq_status_t s) {
     case NQ_ERR_TIMEOUT: return "device-side wait timed out";
     case NQ_ERR_WORKSPACE: return "workspace missing or too small";
     case NQ_ERR_ALIGNMENT: return "pointer or stride not 16-byte aligned";
+    case NQ_ERR_TOO_LARGE: return "problem exceeds the library's built-in scratch size";
   }
   return "unknown status";
 }
