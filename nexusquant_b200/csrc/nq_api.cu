@@ -2,7 +2,9 @@
 // Every function validates its arguments on the host, launches stream-ordered
 // work, never throws and never allocates device memory.
 #include <cmath>
+#include <algorithm>
 #include <cstring>
+#include <vector>
 
 #include "../../include/nexusquant_b200.h"
 #include "nq_internal.h"
@@ -91,10 +93,22 @@ nq_status_t nq_compress_layers(const nq_compress_params_t* p, nq_stream_t stream
   a.rotate = p->rotate;
   a.error_flag = p->error_flag;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  for (int l0 = 0; l0 < p->n_layers; l0 += kMaxLayersPerLaunch) {
-    const int n = std::min(kMaxLayersPerLaunch, p->n_layers - l0);
+  // one launch per (key format, value format) group of layers, at most kMaxLayersPerLaunch each
+  auto fmt = [](int levels) { return levels <= 4 ? 0 : (levels == 8 ? 1 : 2); };
+  std::vector<int> order(p->n_layers);
+  for (int l = 0; l < p->n_layers; ++l) order[l] = l;
+  std::stable_sort(order.begin(), order.end(), [&](int x, int y) {
+    return fmt(p->layers[x].key_levels) * 3 + fmt(p->layers[x].value_levels) <
+           fmt(p->layers[y].key_levels) * 3 + fmt(p->layers[y].value_levels);
+  });
+  for (int l0 = 0; l0 < p->n_layers;) {
+    const int key0 = fmt(p->layers[order[l0]].key_levels) * 3 + fmt(p->layers[order[l0]].value_levels);
+    int n = 0;
+    while (l0 + n < p->n_layers && n < kMaxLayersPerLaunch &&
+           fmt(p->layers[order[l0 + n]].key_levels) * 3 + fmt(p->layers[order[l0 + n]].value_levels) == key0)
+      ++n;
     for (int i = 0; i < n; ++i) {
-      const nq_layer_io_t& L = p->layers[l0 + i];
+      const nq_layer_io_t& L = p->layers[order[l0 + i]];
       nq::LayerIO& d = a.layers[i];
       d.k = L.k; d.v = L.v; d.k_codes = L.k_codes; d.v_codes = L.v_codes;
       d.k_scales = L.k_scales; d.v_scales = L.v_scales;
@@ -104,6 +118,7 @@ nq_status_t nq_compress_layers(const nq_compress_params_t* p, nq_stream_t stream
     }
     const nq_status_t st = cuda_status(nq::launch_compress(a, n, s, any_out));
     if (st != NQ_OK) return st;
+    l0 += n;
   }
   return NQ_OK;
 }

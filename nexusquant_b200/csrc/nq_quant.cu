@@ -179,169 +179,6 @@ __device__ __forceinline__ void reconstruct_store(float (&x)[DP], float scale, b
 }
 
 // --------------------------------------------------------------------------
-// Compress kernel
-// --------------------------------------------------------------------------
-template <typename TIn, int D, int DP, bool RECON>
-__global__ void __launch_bounds__(kCompressThreads, 3) compress_kernel(const CompressArgs args) {
-  constexpr int kInBytes = InTraits<TIn>::kBytes;
-  constexpr int kRowBytes = D * kInBytes;
-  constexpr int kRowStride = kRowBytes + 16;          // padded: conflict-free 16-byte reads
-  constexpr int DH = D / 2;
-  constexpr int kTabStride = 2 * DH * 4 + 16;         // cos | sin | pad
-  extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ uint64_t bar;
-
-  // ---- which tile
-  const int HG = args.head_group;
-  const int TOK = kCompressThreads / HG;
-  int bid = blockIdx.x;
-  const int t_tiles = (args.n_kept + TOK - 1) / TOK;
-  const int h_groups = (args.heads + HG - 1) / HG;
-  const int tt = bid % t_tiles; bid /= t_tiles;
-  const int hg = bid % h_groups; bid /= h_groups;
-  const int b = bid % args.batch; bid /= args.batch;
-  const int kv = bid & 1;
-  const int layer = bid >> 1;
-  const LayerIO& L = args.layers[layer];
-  const bool key = (kv == 0);
-  const TIn* src = static_cast<const TIn*>(key ? L.k : L.v);
-  if (src == nullptr) return;
-  const int levels = key ? L.key_levels : L.value_levels;
-
-  const int tid = threadIdx.x;
-  const int tok_l = tid / HG, head_l = tid % HG;
-  const int j = tt * TOK + tok_l;
-  const int head = hg * HG + head_l;
-  const int count = args.kept_count ? min(args.kept_count[b], args.n_kept) : args.n_kept;
-  const bool valid = (j < count) && (head < args.heads);
-
-  uint8_t* rows = smem;
-  uint8_t* tab = smem + kCompressThreads * kRowStride;
-
-  if (tid == 0) {
-    mbar_init(&bar, 1);
-    fence_mbar_init();
-    int vrows = 0, vtok = 0;
-    for (int tl = 0; tl < TOK; ++tl) {
-      const int jj = tt * TOK + tl;
-      if (jj >= count) break;
-      ++vtok;
-      vrows += min(HG, args.heads - hg * HG);
-    }
-    uint32_t bytes = static_cast<uint32_t>(vrows) * kRowBytes;
-    if (key) bytes += static_cast<uint32_t>(vtok) * (2 * DH * 4);
-    mbar_arrive_expect_tx(&bar, bytes);
-  }
-  __syncthreads();
-
-  const int src_row = valid ? (args.kept_idx ? args.kept_idx[(int64_t)b * args.n_kept + j] : j) : 0;
-  const int pos = valid ? (args.positions ? args.positions[(int64_t)b * args.n_kept + j] : src_row) : 0;
-  if (valid) {
-    const TIn* g = src + (int64_t)b * args.in_stride_b + (int64_t)head * args.in_stride_h +
-                   (int64_t)src_row * args.in_stride_t;
-    bulk_g2s(rows + tid * kRowStride, g, kRowBytes, &bar);
-    if (key && head_l == 0) {
-      uint8_t* trow = tab + tok_l * kTabStride;
-      bulk_g2s(trow, args.rope_cos + (int64_t)pos * DH, DH * 4, &bar);
-      bulk_g2s(trow + DH * 4, args.rope_sin + (int64_t)pos * DH, DH * 4, &bar);
-    }
-  }
-  if (!mbar_wait(&bar, 0)) {
-    if (args.error_flag) atomicExch(args.error_flag, 1);
-    return;
-  }
-  if (!valid) return;
-
-  // ---- load, widen, inverse RoPE
-  float x[DP];
-  const TIn* r = reinterpret_cast<const TIn*>(rows + tid * kRowStride);
-#pragma unroll
-  for (int k = 0; k < D / 8; ++k) load8(r + 8 * k, &x[8 * k]);
-#pragma unroll
-  for (int i = D; i < DP; ++i) x[i] = 0.0f;
-  if (key) {
-    const float* cs = reinterpret_cast<const float*>(tab + tok_l * kTabStride);
-    const float* sn = cs + DH;
-#pragma unroll
-    for (int i = 0; i < DH; i += 4) {
-      const float4 c4 = *reinterpret_cast<const float4*>(cs + i);
-      const float4 s4 = *reinterpret_cast<const float4*>(sn + i);
-      const float cc[4] = {c4.x, c4.y, c4.z, c4.w};
-      const float ss[4] = {s4.x, s4.y, s4.z, s4.w};
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const float x1 = x[i + u], x2 = x[i + u + DH];
-        x[i + u] = __fadd_rn(__fmul_rn(x1, cc[u]), __fmul_rn(x2, ss[u]));
-        x[i + u + DH] = __fsub_rn(__fmul_rn(x2, cc[u]), __fmul_rn(x1, ss[u]));
-      }
-    }
-  }
-
-  // ---- rotate, scale
-  float amax = 0.0f;
-  if (args.rotate) {
-    fwht_regs<DP>(x);
-    constexpr float kH = hadamard_entry(DP);
-#pragma unroll
-    for (int i = 0; i < DP; ++i) {
-      x[i] = __fmul_rn(x[i], kH);
-      amax = fmaxf(amax, fabsf(x[i]));
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < DP; ++i) amax = fmaxf(amax, fabsf(x[i]));
-  }
-  amax = fmaxf(amax, 1e-8f);
-  const float sc = __fmul_rn(amax, 2.0f / static_cast<float>(levels));
-  const float rcp = __frcp_rn(sc);
-
-  // ---- lattice
-  constexpr int kWords = DP / 4;  // enough for the largest format (int8: DP bytes)
-  uint32_t w[kWords];
-#pragma unroll
-  for (int i = 0; i < kWords; ++i) w[i] = 0u;
-#pragma unroll
-  for (int gi = 0; gi < DP / 8; ++gi) {
-    float n[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) n[i] = div_by(x[8 * gi + i], sc, rcp);
-    int c[8];
-    e8_group(n, levels, c);
-    pack_group<DP>(w, gi, c, levels);
-    if (RECON) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) x[8 * gi + i] = static_cast<float>(c[i]);
-    }
-  }
-
-  // ---- outputs
-  const int64_t vrow = ((int64_t)b * args.heads + head) * args.n_kept + j;
-  uint8_t* codes = key ? L.k_codes : L.v_codes;
-  if (codes) {
-    if (levels <= 4) store_row<DP / 2>(codes + vrow * (DP / 2), w);
-    else if (levels == 8) store_row<DP * 5 / 8>(codes + vrow * (DP * 5 / 8), w);
-    else store_row<DP>(codes + vrow * DP, w);
-  }
-  uint16_t* sc16 = key ? L.k_scales : L.v_scales;
-  if (sc16) sc16[vrow] = __half_as_ushort(__float2half_rn(sc));
-  float* sc32 = key ? L.k_scales_f32 : L.v_scales_f32;
-  if (sc32) sc32[vrow] = sc;
-  if (RECON) {
-    uint16_t* out = key ? L.k_out : L.v_out;
-    if (out) {
-      const int orow = args.out_row_mode == 1 ? j : src_row;
-      int opos = pos;
-      if (args.out_positions) opos = args.out_positions[(int64_t)b * args.n_kept + j];
-      else if (args.out_row_mode == 1) opos = j;
-      __half* o = reinterpret_cast<__half*>(out) + (int64_t)b * args.out_stride_b + (int64_t)head * args.out_stride_h +
-                  (int64_t)orow * args.out_stride_t;
-      reconstruct_store<D, DP>(x, sc, key, args.rope_cos + (int64_t)opos * DH, args.rope_sin + (int64_t)opos * DH,
-                               args.key_sharpen, o, args.rotate != 0);
-    }
-  }
-}
-
-// --------------------------------------------------------------------------
 // Dequantize kernel: one thread per vector, codes read straight from global.
 // --------------------------------------------------------------------------
 template <int D, int DP>
@@ -432,41 +269,6 @@ __global__ void __launch_bounds__(kCompressThreads, 3) decompress_kernel(const D
 // --------------------------------------------------------------------------
 // Launchers
 // --------------------------------------------------------------------------
-template <typename TIn, int D, int DP>
-static cudaError_t launch_compress_t(const CompressArgs& a, int n_blocks, cudaStream_t s, bool recon) {
-  constexpr int kRowStride = D * InTraits<TIn>::kBytes + 16;
-  constexpr int kTabStride = 2 * (D / 2) * 4 + 16;
-  const int tok = kCompressThreads / a.head_group;
-  const size_t smem = (size_t)kCompressThreads * kRowStride + (size_t)tok * kTabStride;
-  auto kern = recon ? compress_kernel<TIn, D, DP, true> : compress_kernel<TIn, D, DP, false>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
-  kern<<<n_blocks, kCompressThreads, smem, s>>>(a);
-  return cudaGetLastError();
-}
-
-template <typename TIn>
-static cudaError_t dispatch_dim(const CompressArgs& a, int n_blocks, cudaStream_t s, bool recon) {
-  if (a.head_dim == 128 && a.head_dim_padded == 128) return launch_compress_t<TIn, 128, 128>(a, n_blocks, s, recon);
-  if (a.head_dim == 96 && a.head_dim_padded == 128) return launch_compress_t<TIn, 96, 128>(a, n_blocks, s, recon);
-  if (a.head_dim == 64 && a.head_dim_padded == 64) return launch_compress_t<TIn, 64, 64>(a, n_blocks, s, recon);
-  return cudaErrorInvalidValue;
-}
-
-cudaError_t launch_compress(const CompressArgs& a, int n_layers, cudaStream_t s, bool recon) {
-  const int tok = kCompressThreads / a.head_group;
-  const long long blocks = (long long)n_layers * 2 * a.batch * ((a.heads + a.head_group - 1) / a.head_group) *
-                           ((a.n_kept + tok - 1) / tok);
-  if (blocks <= 0) return cudaSuccess;
-  if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
-  switch (a.in_dtype) {
-    case 0: return dispatch_dim<__half>(a, (int)blocks, s, recon);
-    case 1: return dispatch_dim<__nv_bfloat16>(a, (int)blocks, s, recon);
-    case 2: return dispatch_dim<float>(a, (int)blocks, s, recon);
-  }
-  return cudaErrorInvalidValue;
-}
-
 cudaError_t launch_decompress(const DecompressArgs& a, int n_layers, cudaStream_t s) {
   const int tok = kCompressThreads / a.head_group;
   const long long blocks = (long long)n_layers * 2 * a.batch * ((a.heads + a.head_group - 1) / a.head_group) *
