@@ -1,0 +1,6 @@
+// Compress kernels for __nv_bfloat16 caches (see nq_compress.cuh).
+#include "nq_compress.cuh"
+
+namespace nq {
+template cudaError_t launch_compress_t<__nv_bfloat16>(const CompressArgs&, int, long long, int, int, cudaStream_t, bool);
+}  // namespace nq

@@ -41,8 +41,8 @@
  *      which with |x_i - B_i| = 1/2 - g_i becomes
  *          choose B  <=>  sum_i g_i + odd * (1 - 2 g_min) > 2,
  *      where g_i = |x_i - round(x_i)| (exact in fp32), odd is the parity of the
- *      rounded sum and g_min the smallest gap.  The sum is taken in fp32 in
- *      index order.  (Derivation: for each coordinate |B_i - A_i| = 1/2, so
+ *      rounded sum and g_min the smallest gap.  The sum is taken in fp32 as
+ *      ((g0+g1)+(g2+g3))+((g4+g5)+(g6+g7)).  (Derivation: for each coordinate |B_i - A_i| = 1/2, so
  *      (x-B)^2 - (x-A)^2 = 1/4 - g; the parity fix moves one coordinate from
  *      gap g_min to 1 - g_min, adding 1 - 2 g_min to d_int.)
  *
@@ -100,8 +100,7 @@ static void e8_group(const float *x, int levels, int8_t *code) {
         bp[i] = (int)(sb - NQO_MAGIC);      /* round-half-even(fl(x - 0.5)) */
         par += a[i];
     }
-    float gsum = g[0];
-    for (int i = 1; i < 8; ++i) gsum = gsum + g[i];
+    float gsum = ((g[0] + g[1]) + (g[2] + g[3])) + ((g[4] + g[5]) + (g[6] + g[7]));  /* pairwise */
     int idx = 0;
     float gmin = g[0];
     for (int i = 1; i < 8; ++i)
