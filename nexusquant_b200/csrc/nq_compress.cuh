@@ -10,19 +10,20 @@
 // nexusquant/core/rope_utils.py:75-122, nexusquant/integrations/vllm_backend.py:267-316.
 //
 // Design:
-//  * One thread owns one vector.  Coordinates are held as pairs
+//  * Two threads own one vector.  Coordinates are held as pairs
 //    P[j] = {x[j], x[j + d_p/2]} in 64-bit registers so the RoPE products, the
-//    first log2(d_p)-1 butterfly stages, the scale, the division and half of
-//    the lattice arithmetic run as sm_100 packed f32x2 instructions (two
-//    IEEE-rounded fp32 results per instruction, bit-identical to scalar code).
+//    butterfly stages, the scale, the division and half of the lattice
+//    arithmetic run as sm_100 packed f32x2 instructions (two IEEE-rounded fp32
+//    results per instruction, bit-identical to scalar code).  Each thread holds
+//    half of the pairs; one butterfly stage crosses the thread pair (shuffle).
 //    Group g (low lanes) and group g + d_p/16 (high lanes) go through the
 //    lattice step together.
 //  * K vs V and the packing format are template parameters, so the per-vector
 //    code is one branch-free basic block.
-//  * Persistent CTAs (2 per SM) walk the tile list; each has a two-stage
-//    shared-memory pipeline: while tile i is computed, the rows of tile i+1 are
-//    in flight through the TMA engine (cp.async.bulk, no multicast).
-//  * A tile is HG heads x (128/HG) tokens of one (layer, K|V, batch); threads of
+//  * Persistent CTAs walk the tile list; each has a two-stage shared-memory
+//    pipeline: while tile i is computed, the rows of tile i+1 are in flight
+//    through the TMA engine (cp.async.bulk, no multicast).
+//  * A tile is HG heads x (64/HG) tokens of one (layer, K|V, batch); threads of
 //    a warp that share a token read the same RoPE row (shared-memory broadcast).
 #include "nq_common.cuh"
 #include "nq_internal.h"
@@ -151,20 +152,33 @@ __device__ __forceinline__ void pack_fields(uint32_t* w, int g, const int (&f)[8
   }
 }
 
-template <int BYTES>
-__device__ __forceinline__ void store_words(uint8_t* dst, const uint32_t* w) {
-  if constexpr ((BYTES & 15) == 0) {
-    uint4* d = reinterpret_cast<uint4*>(dst);
+
+// Store BYTES bytes of words to dst using G-byte stores (G divides BYTES and dst's alignment).
+template <int BYTES, int G>
+__device__ __forceinline__ void store_region(uint8_t* dst, const uint32_t* w) {
+  if constexpr (G == 16) {
 #pragma unroll
-    for (int k = 0; k < BYTES / 16; ++k) d[k] = make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+    for (int k = 0; k < BYTES / 16; ++k)
+      reinterpret_cast<uint4*>(dst)[k] = make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+  } else if constexpr (G == 8) {
+#pragma unroll
+    for (int k = 0; k < BYTES / 8; ++k) reinterpret_cast<uint2*>(dst)[k] = make_uint2(w[2 * k], w[2 * k + 1]);
+  } else if constexpr (G == 4) {
+#pragma unroll
+    for (int k = 0; k < BYTES / 4; ++k) reinterpret_cast<uint32_t*>(dst)[k] = w[k];
   } else {
-    uint2* d = reinterpret_cast<uint2*>(dst);
 #pragma unroll
-    for (int k = 0; k < BYTES / 8; ++k) d[k] = make_uint2(w[2 * k], w[2 * k + 1]);
+    for (int k = 0; k < BYTES / 2; ++k)
+      reinterpret_cast<uint16_t*>(dst)[k] = static_cast<uint16_t>(w[k >> 1] >> (16 * (k & 1)));
   }
 }
 
-// Fake-quant reconstruction from the fields (codes + 8), written as fp16.
+__host__ __device__ constexpr int largest_pow2_div(int a) { return a % 16 == 0 ? 16 : a % 8 == 0 ? 8 : a % 4 == 0 ? 4 : 2; }
+__host__ __device__ constexpr int gcd_pow2(int a, int b) {
+  return largest_pow2_div(a) < largest_pow2_div(b) ? largest_pow2_div(a) : largest_pow2_div(b);
+}
+
+// Fake-quant reconstruction of a full vector of codes (as floats), written as fp16.
 template <int D, int DP>
 __device__ __forceinline__ void recon_store(float (&x)[DP], float sc, bool key, const float* cosr,
                                             const float* sinr, float sharpen, bool rotate, __half* out) {
@@ -214,22 +228,28 @@ __device__ __forceinline__ void recon_store(float (&x)[DP], float sc, bool key, 
 }
 
 // --------------------------------------------------------------------------
-// Tile geometry shared by the load and compute phases.
+// Tile geometry: a tile is HG heads x (kCompressVecs/HG) tokens of one
+// (layer, K|V, batch); vector v of the tile is owned by threads 2v and 2v+1.
 // --------------------------------------------------------------------------
 struct Tile {
   int layer, kv, b, hg, tt;
 };
 
-__device__ __forceinline__ Tile decode_tile(const CompressArgs& a, int n_layers, long long t) {
-  const int TOK = kCompressThreads / a.head_group;
+// Decoded once per tile and iteration (32-bit: the host keeps the tile count below 2^31).
+__device__ __forceinline__ Tile decode_tile(const CompressArgs& a, int n_layers, int t) {
+  const int TOK = kCompressVecs / a.head_group;
   const int t_tiles = (a.n_kept + TOK - 1) / TOK;
   const int h_groups = (a.heads + a.head_group - 1) / a.head_group;
   Tile r;
-  r.tt = (int)(t % t_tiles); t /= t_tiles;
-  r.hg = (int)(t % h_groups); t /= h_groups;
-  r.b = (int)(t % a.batch); t /= a.batch;
-  r.layer = (int)(t % n_layers); t /= n_layers;
-  r.kv = (int)t;  // K tiles first, then V tiles
+  int q = t / t_tiles;
+  r.tt = t - q * t_tiles;
+  t = q; q = t / h_groups;
+  r.hg = t - q * h_groups;
+  t = q; q = t / a.batch;
+  r.b = t - q * a.batch;
+  t = q; q = t / n_layers;
+  r.layer = t - q * n_layers;
+  r.kv = q;  // K tiles first, then V tiles
   return r;
 }
 
@@ -238,33 +258,31 @@ struct Smem {
   static constexpr int kRowBytes = D * InTraits<TIn>::kBytes;
   static constexpr int kRowStride = kRowBytes + 16;  // padded: conflict-free 16-byte reads
   static constexpr int kTabStride = 2 * (D / 2) * 4 + 16;
-  static constexpr int kRows = kCompressThreads * kRowStride;
+  static constexpr int kRows = kCompressVecs * kRowStride;
   // rows + one RoPE row per token of the tile, rounded to 128 bytes
   __host__ __device__ static constexpr int stage(int head_group) {
-    return (kRows + (kCompressThreads / head_group) * kTabStride + 127) & ~127;
+    return (kRows + (kCompressVecs / head_group) * kTabStride + 127) & ~127;
   }
 };
 
-// Issue the TMA copies of one tile into a stage (all threads; thread 0 posts the byte count first).
+// Issue the TMA copies of one tile into a stage (thread 2v copies row v; thread 0 posts the bytes first).
 template <typename TIn, int D>
-__device__ __forceinline__ void issue_tile(const CompressArgs& a, int n_layers, long long tile, uint8_t* stage,
-                                           uint64_t* bar) {
+__device__ __forceinline__ void issue_tile(const CompressArgs& a, const Tile& t, uint8_t* stage, uint64_t* bar) {
   using S = Smem<TIn, D>;
-  const Tile t = decode_tile(a, n_layers, tile);
+  if (threadIdx.x & 1) return;
   const LayerIO& L = a.layers[t.layer];
   const bool key = t.kv == 0;
   const TIn* src = static_cast<const TIn*>(key ? L.k : L.v);
-  const int HG = a.head_group, TOK = kCompressThreads / HG;
+  const int HG = a.head_group, TOK = kCompressVecs / HG;
   const int count = a.kept_count ? min(a.kept_count[t.b], a.n_kept) : a.n_kept;
-  const int tid = threadIdx.x;
-  const int tok_l = tid / HG, head_l = tid % HG;
+  const int v = threadIdx.x >> 1;
+  const int tok_l = v / HG, head_l = v % HG;
   const int j = t.tt * TOK + tok_l;
   const int head = t.hg * HG + head_l;
-  const bool valid = src != nullptr && j < count && head < a.heads;
-  if (valid) {
+  if (src != nullptr && j < count && head < a.heads) {
     const int row = a.kept_idx ? a.kept_idx[(int64_t)t.b * a.n_kept + j] : j;
     const TIn* g = src + (int64_t)t.b * a.in_stride_b + (int64_t)head * a.in_stride_h + (int64_t)row * a.in_stride_t;
-    bulk_g2s(stage + tid * S::kRowStride, g, S::kRowBytes, bar);
+    bulk_g2s(stage + v * S::kRowStride, g, S::kRowBytes, bar);
     if (key && head_l == 0) {
       const int pos = a.positions ? a.positions[(int64_t)t.b * a.n_kept + j] : row;
       uint8_t* trow = stage + S::kRows + tok_l * S::kTabStride;
@@ -275,12 +293,11 @@ __device__ __forceinline__ void issue_tile(const CompressArgs& a, int n_layers, 
 }
 
 template <typename TIn, int D>
-__device__ __forceinline__ uint32_t tile_bytes(const CompressArgs& a, int n_layers, long long tile) {
-  const Tile t = decode_tile(a, n_layers, tile);
+__device__ __forceinline__ uint32_t tile_bytes(const CompressArgs& a, const Tile& t) {
   const LayerIO& L = a.layers[t.layer];
   const bool key = t.kv == 0;
   if ((key ? L.k : L.v) == nullptr) return 0;
-  const int HG = a.head_group, TOK = kCompressThreads / HG;
+  const int HG = a.head_group, TOK = kCompressVecs / HG;
   const int count = a.kept_count ? min(a.kept_count[t.b], a.n_kept) : a.n_kept;
   const int toks = max(0, min(TOK, count - t.tt * TOK));
   const int heads = min(HG, a.heads - t.hg * HG);
@@ -290,44 +307,49 @@ __device__ __forceinline__ uint32_t tile_bytes(const CompressArgs& a, int n_laye
 }
 
 // --------------------------------------------------------------------------
-// Per-vector body for one tile (K or V, one packing format).
+// Per-vector body (two threads per vector), one tile of K or V, one format.
+// Thread h of the pair owns pairs P[q] = {x[q], x[q + DP/2]} for q in
+// [h*DP/4, (h+1)*DP/4): all butterfly stages but one are in-thread, the stage
+// of stride DP/4 crosses the pair through one shuffle per register.
 // --------------------------------------------------------------------------
 template <typename TIn, int D, int DP, bool KEY, int FMT, bool RECON>
-__device__ __forceinline__ void compress_tile(const CompressArgs& a, int n_layers, long long tile,
-                                              const uint8_t* stage) {
+__device__ __forceinline__ void compress_tile(const CompressArgs& a, const Tile& t, const uint8_t* stage) {
   using S = Smem<TIn, D>;
-  constexpr int H2 = DP / 2;  // pairs
-  const Tile t = decode_tile(a, n_layers, tile);
+  constexpr int H2 = DP / 2;  // pairs per vector
+  constexpr int HP = H2 / 2;  // pairs per thread
   const LayerIO& L = a.layers[t.layer];
+  if ((KEY ? L.k : L.v) == nullptr) return;  // uniform over the CTA
   const int levels = KEY ? L.key_levels : L.value_levels;
-  const int HG = a.head_group, TOK = kCompressThreads / HG;
+  const int HG = a.head_group, TOK = kCompressVecs / HG;
   const int count = a.kept_count ? min(a.kept_count[t.b], a.n_kept) : a.n_kept;
-  const int tid = threadIdx.x;
-  const int tok_l = tid / HG, head_l = tid % HG;
+  const int v = threadIdx.x >> 1, h = threadIdx.x & 1;
+  const int tok_l = v / HG, head_l = v % HG;
   const int j = t.tt * TOK + tok_l;
   const int head = t.hg * HG + head_l;
-  if (j >= count || head >= a.heads || (KEY ? L.k : L.v) == nullptr) return;
+  // both threads of every pair run the whole body (they exchange data); invalid ones store nothing
+  const bool valid = j < count && head < a.heads;
 
-  // ---- load, widen, inverse RoPE -> pairs P[q] = {x[q], x[q + DP/2]}
-  u64 P[H2];
-  const TIn* r = reinterpret_cast<const TIn*>(stage + tid * S::kRowStride);
+  // ---- load, widen, inverse RoPE -> this thread's pairs
+  u64 P[HP];
+  const TIn* r = reinterpret_cast<const TIn*>(stage + v * S::kRowStride);
   const float* cs = reinterpret_cast<const float*>(stage + S::kRows + tok_l * S::kTabStride);
   const float* sn = cs + D / 2;
+  const int q0 = h * HP;
   if constexpr (D == DP) {
 #pragma unroll
-    for (int k = 0; k < H2 / 8; ++k) {
+    for (int k = 0; k < HP / 8; ++k) {
       float lo[8], hi[8];
-      load8(r + 8 * k, lo);
-      load8(r + H2 + 8 * k, hi);
+      load8(r + q0 + 8 * k, lo);
+      load8(r + H2 + q0 + 8 * k, hi);
 #pragma unroll
       for (int i = 0; i < 8; ++i) P[8 * k + i] = pk(lo[i], hi[i]);
     }
     if constexpr (KEY) {
       // pair (q, q + D/2) is P[q]: y1 = x1 c + x2 s, y2 = x2 c - x1 s
 #pragma unroll
-      for (int q = 0; q < H2; q += 4) {
-        const float4 c4 = *reinterpret_cast<const float4*>(cs + q);
-        const float4 s4 = *reinterpret_cast<const float4*>(sn + q);
+      for (int q = 0; q < HP; q += 4) {
+        const float4 c4 = *reinterpret_cast<const float4*>(cs + q0 + q);
+        const float4 s4 = *reinterpret_cast<const float4*>(sn + q0 + q);
         const float cc[4] = {c4.x, c4.y, c4.z, c4.w};
         const float ss[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
@@ -340,7 +362,8 @@ __device__ __forceinline__ void compress_tile(const CompressArgs& a, int n_layer
       }
     }
   } else {
-    // D < DP (96 -> 128): RoPE pairs (i, i + D/2) do not line up with the register pairs
+    // D < DP (96 -> 128): RoPE pairs (i, i + D/2) straddle the two threads, so each
+    // thread rotates the whole row and keeps its own coordinates.
     float x[D];
 #pragma unroll
     for (int k = 0; k < D / 8; ++k) load8(r + 8 * k, &x[8 * k]);
@@ -354,64 +377,81 @@ __device__ __forceinline__ void compress_tile(const CompressArgs& a, int n_layer
       }
     }
 #pragma unroll
-    for (int q = 0; q < H2; ++q) P[q] = pk(x[q], q + H2 < D ? x[q + H2] : 0.0f);
+    for (int q = 0; q < HP; ++q) {
+      const float lo0 = x[q], lo1 = x[q + HP];
+      const float hi0 = q + H2 < D ? x[q + H2] : 0.0f;
+      const float hi1 = q + HP + H2 < D ? x[q + HP + H2] : 0.0f;
+      P[q] = h ? pk(lo1, hi1) : pk(lo0, hi0);
+    }
   }
 
-  // ---- rotate (stages 1 .. DP/4 on pairs, stage DP/2 inside each pair), scale
+  // ---- rotate: stages 1 .. HP/2 in-thread, stage HP across the pair, stage H2 inside each register
   float amax = 0.0f;
   if (a.rotate) {
 #pragma unroll
-    for (int h = 1; h < H2; h <<= 1) {
+    for (int st = 1; st < HP; st <<= 1) {
 #pragma unroll
-      for (int q = 0; q < H2; ++q) {
-        if ((q & h) == 0) {
-          const u64 u = P[q], v = P[q + h];
-          P[q] = add2(u, v);
-          P[q + h] = sub2(u, v);
+      for (int q = 0; q < HP; ++q) {
+        if ((q & st) == 0) {
+          const u64 u = P[q], w2 = P[q + st];
+          P[q] = add2(u, w2);
+          P[q + st] = sub2(u, w2);
         }
       }
     }
+    // lower thread: a + b; upper thread: a - b  (a = lower thread's value)  == fma(mine, +-1, other)
+    const float sg = h ? -1.0f : 1.0f;
+    const u64 sg2 = pk(sg, sg);
+#pragma unroll
+    for (int q = 0; q < HP; ++q) {
+      const u64 o = __shfl_xor_sync(0xffffffffu, P[q], 1);
+      P[q] = fma2(P[q], sg2, o);
+    }
     const u64 hh = pk(hadamard_entry(DP), hadamard_entry(DP));
 #pragma unroll
-    for (int q = 0; q < H2; ++q) {
-      float u, v;
-      upk(P[q], u, v);
-      P[q] = mul2(pk(__fadd_rn(u, v), __fsub_rn(u, v)), hh);
+    for (int q = 0; q < HP; ++q) {
+      float u, w2;
+      upk(P[q], u, w2);
+      P[q] = mul2(pk(__fadd_rn(u, w2), __fsub_rn(u, w2)), hh);
       float y0, y1;
       upk(P[q], y0, y1);
       amax = max3(amax, fabsf(y0), fabsf(y1));
     }
   } else {
 #pragma unroll
-    for (int q = 0; q < H2; ++q) {
+    for (int q = 0; q < HP; ++q) {
       float y0, y1;
       upk(P[q], y0, y1);
       amax = max3(amax, fabsf(y0), fabsf(y1));
     }
   }
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
   amax = fmaxf(amax, 1e-8f);
   const float sc = __fmul_rn(amax, 2.0f / static_cast<float>(levels));
   const float rcp = __frcp_rn(sc);
   const u64 r2 = pk(rcp, rcp), nsc2 = pk(-sc, -sc);
   const u64 M2 = pk(kMagic, kMagic), half2 = pk(0.5f, 0.5f);
 
-  // ---- lattice: groups g (low lanes) and g + DP/16 (high lanes) together
-  constexpr int G = DP / 8;
-  uint32_t w[Fmt<FMT, DP>::kWords];
+  // ---- lattice: this thread's groups g (low lanes) and g + DP/16 (high lanes)
+  constexpr int GT = HP / 8;                  // groups per lane type per thread
+  constexpr int GB = FMT == 0 ? 4 : (FMT == 1 ? 5 : 8);  // bytes per group
+  constexpr int REG = GT * GB;                // bytes per region (low / high)
+  constexpr int RW = (REG + 3) / 4;           // words per region
+  uint32_t wl[RW], wh[RW];
 #pragma unroll
-  for (int i = 0; i < Fmt<FMT, DP>::kWords; ++i) w[i] = 0u;
-  float xr[RECON ? DP : 1];
+  for (int i = 0; i < RW; ++i) { wl[i] = 0u; wh[i] = 0u; }
+  int fl_all[RECON ? HP : 1][8], fh_all[RECON ? HP : 1][8];
 #pragma unroll
-  for (int g = 0; g < G / 2; ++g) {
+  for (int g = 0; g < GT; ++g) {
     float elo[8], ehi[8];
     uint32_t slo[8], shi[8], blo[8], bhi[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const u64 y = P[8 * g + i];
       // correctly rounded y / sc (Markstein): q = y r; rem = y - q sc; q + rem r
-      const u64 q0 = mul2(y, r2);
-      const u64 rem = fma2(q0, nsc2, y);
-      const u64 n = fma2(rem, r2, q0);
+      const u64 q1 = mul2(y, r2);
+      const u64 rem = fma2(q1, nsc2, y);
+      const u64 n = fma2(rem, r2, q1);
       const u64 s = add2(n, M2);
       const u64 e = sub2(n, sub2(s, M2));
       const u64 sb = add2(sub2(n, half2), M2);
@@ -425,14 +465,11 @@ __device__ __forceinline__ void compress_tile(const CompressArgs& a, int n_layer
     int flo[8], fhi[8];
     e8_fields(elo, slo, blo, levels, flo);
     e8_fields(ehi, shi, bhi, levels, fhi);
-    pack_fields<FMT, DP>(w, g, flo);
-    pack_fields<FMT, DP>(w, g + G / 2, fhi);
+    pack_fields<FMT, DP>(wl, g, flo);
+    pack_fields<FMT, DP>(wh, g, fhi);
     if constexpr (RECON) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        xr[8 * g + i] = static_cast<float>(flo[i] - 8);
-        xr[8 * (g + G / 2) + i] = static_cast<float>(fhi[i] - 8);
-      }
+      for (int i = 0; i < 8; ++i) { fl_all[g][i] = flo[i]; fh_all[g][i] = fhi[i]; }
     }
   }
 
@@ -440,76 +477,105 @@ __device__ __forceinline__ void compress_tile(const CompressArgs& a, int n_layer
   const int64_t vrow = ((int64_t)t.b * a.heads + head) * a.n_kept + j;
   uint8_t* codes = KEY ? L.k_codes : L.v_codes;
   constexpr int PB = Fmt<FMT, DP>::kBytes;
-  if (codes) store_words<PB>(codes + vrow * PB, w);
-  uint16_t* sc16 = KEY ? L.k_scales : L.v_scales;
-  if (sc16) sc16[vrow] = __half_as_ushort(__float2half_rn(sc));
-  float* sc32 = KEY ? L.k_scales_f32 : L.v_scales_f32;
-  if (sc32) sc32[vrow] = sc;
+  constexpr int HOFF = (H2 / 8) * GB;  // byte offset of the high-lane groups
+  constexpr int G = gcd_pow2(gcd_pow2(REG, HOFF), PB);
+  if (valid && codes) {
+    uint8_t* row = codes + vrow * PB;
+    store_region<REG, G>(row + h * REG, wl);
+    store_region<REG, G>(row + HOFF + h * REG, wh);
+  }
+  if (valid && h == 0) {
+    uint16_t* sc16 = KEY ? L.k_scales : L.v_scales;
+    if (sc16) sc16[vrow] = __half_as_ushort(__float2half_rn(sc));
+    float* sc32 = KEY ? L.k_scales_f32 : L.v_scales_f32;
+    if (sc32) sc32[vrow] = sc;
+  }
   if constexpr (RECON) {
     uint16_t* out = KEY ? L.k_out : L.v_out;
     if (out) {
-      const int src_row = a.kept_idx ? a.kept_idx[(int64_t)t.b * a.n_kept + j] : j;
-      const int pos = a.positions ? a.positions[(int64_t)t.b * a.n_kept + j] : src_row;
-      const int orow = a.out_row_mode == 1 ? j : src_row;
-      int opos = pos;
-      if (a.out_positions) opos = a.out_positions[(int64_t)t.b * a.n_kept + j];
-      else if (a.out_row_mode == 1) opos = j;
-      __half* o = reinterpret_cast<__half*>(out) + (int64_t)t.b * a.out_stride_b + (int64_t)head * a.out_stride_h +
-                  (int64_t)orow * a.out_stride_t;
-      recon_store<D, DP>(xr, sc, KEY, a.rope_cos + (int64_t)opos * (D / 2), a.rope_sin + (int64_t)opos * (D / 2),
-                         a.key_sharpen, a.rotate != 0, o);
+      // assemble the full code vector in the lower thread of the pair
+      float x[DP];
+#pragma unroll
+      for (int g = 0; g < GT; ++g)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int mine_l = fl_all[g][i] - 8, mine_h = fh_all[g][i] - 8;
+          const int oth_l = __shfl_xor_sync(0xffffffffu, mine_l, 1);
+          const int oth_h = __shfl_xor_sync(0xffffffffu, mine_h, 1);
+          const int q = 8 * g + i;
+          x[q] = static_cast<float>(mine_l);             // valid in the lower thread
+          x[q + HP] = static_cast<float>(oth_l);
+          x[q + H2] = static_cast<float>(mine_h);
+          x[q + HP + H2] = static_cast<float>(oth_h);
+        }
+      if (valid && h == 0) {
+        const int src_row = a.kept_idx ? a.kept_idx[(int64_t)t.b * a.n_kept + j] : j;
+        const int pos = a.positions ? a.positions[(int64_t)t.b * a.n_kept + j] : src_row;
+        const int orow = a.out_row_mode == 1 ? j : src_row;
+        int opos = pos;
+        if (a.out_positions) opos = a.out_positions[(int64_t)t.b * a.n_kept + j];
+        else if (a.out_row_mode == 1) opos = j;
+        __half* o = reinterpret_cast<__half*>(out) + (int64_t)t.b * a.out_stride_b +
+                    (int64_t)head * a.out_stride_h + (int64_t)orow * a.out_stride_t;
+        recon_store<D, DP>(x, sc, KEY, a.rope_cos + (int64_t)opos * (D / 2), a.rope_sin + (int64_t)opos * (D / 2),
+                           a.key_sharpen, a.rotate != 0, o);
+      }
     }
   }
 }
 
 // --------------------------------------------------------------------------
-// Persistent kernel: two-stage TMA pipeline over the tile list.
+// Persistent kernel: 1- or 2-stage TMA pipeline over the tile list.
 // --------------------------------------------------------------------------
 template <typename TIn, int D, int DP, int FMTK, int FMTV, bool RECON>
-__global__ void __launch_bounds__(kCompressThreads, 2) compress_kernel(const CompressArgs args, int n_layers,
-                                                                        long long n_tiles, int ns) {
+__global__ void __launch_bounds__(kCompressThreads, 4) compress_kernel(const CompressArgs args, int n_layers,
+                                                                        int n_tiles, int ns) {
   using S = Smem<TIn, D>;
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint64_t bar[2];
-  const long long first = blockIdx.x;
+  const int first = blockIdx.x;
   if (first >= n_tiles) return;
+  const int stage_bytes = S::stage(args.head_group);
+  Tile cur = decode_tile(args, n_layers, first);
   if (threadIdx.x == 0) {
     mbar_init(&bar[0], 1);
     mbar_init(&bar[1], 1);
     fence_mbar_init();
-    mbar_arrive_expect_tx(&bar[0], tile_bytes<TIn, D>(args, n_layers, first));
+    mbar_arrive_expect_tx(&bar[0], tile_bytes<TIn, D>(args, cur));
   }
   __syncthreads();
-  issue_tile<TIn, D>(args, n_layers, first, smem, &bar[0]);
+  issue_tile<TIn, D>(args, cur, smem, &bar[0]);
   int it = 0;
   // ns = 2: tile i+1 is loaded into the other stage while tile i is computed;
   // ns = 1 (rows too large for two stages): load and compute alternate.
-  for (long long tile = first; tile < n_tiles; tile += gridDim.x, ++it) {
+  for (int tile = first; tile < n_tiles; tile += gridDim.x, ++it) {
     const int s = ns == 2 ? (it & 1) : 0;
     const uint32_t ph = ns == 2 ? ((it >> 1) & 1) : (it & 1);
-    const long long next = tile + gridDim.x;
-    // everyone has finished the tile that used stage s^1 (previous iteration) here
-    __syncthreads();
-    if (ns == 2 && next < n_tiles) {
-      if (threadIdx.x == 0) mbar_arrive_expect_tx(&bar[s ^ 1], tile_bytes<TIn, D>(args, n_layers, next));
+    const int next = tile + (int)gridDim.x;
+    const bool has_next = next < n_tiles;
+    Tile nt = cur;
+    if (has_next) nt = decode_tile(args, n_layers, next);
+    __syncthreads();  // the tile that used stage s^1 (previous iteration) is finished
+    if (ns == 2 && has_next) {
+      if (threadIdx.x == 0) mbar_arrive_expect_tx(&bar[s ^ 1], tile_bytes<TIn, D>(args, nt));
       __syncthreads();
-      issue_tile<TIn, D>(args, n_layers, next, smem + (s ^ 1) * S::stage(args.head_group), &bar[s ^ 1]);
+      issue_tile<TIn, D>(args, nt, smem + (s ^ 1) * stage_bytes, &bar[s ^ 1]);
     }
     if (!mbar_wait(&bar[s], ph)) {
       if (args.error_flag) atomicExch(args.error_flag, 1);
-      if (ns == 2 && next < n_tiles) mbar_wait(&bar[s ^ 1], ((it + 1) >> 1) & 1);  // let in-flight copies land
+      if (ns == 2 && has_next) mbar_wait(&bar[s ^ 1], ((it + 1) >> 1) & 1);  // let in-flight copies land
       return;
     }
-    const uint8_t* stage = smem + s * S::stage(args.head_group);
-    const Tile t = decode_tile(args, n_layers, tile);
-    if (t.kv == 0) compress_tile<TIn, D, DP, true, FMTK, RECON>(args, n_layers, tile, stage);
-    else compress_tile<TIn, D, DP, false, FMTV, RECON>(args, n_layers, tile, stage);
-    if (ns == 1 && next < n_tiles) {
+    const uint8_t* stage = smem + s * stage_bytes;
+    if (cur.kv == 0) compress_tile<TIn, D, DP, true, FMTK, RECON>(args, cur, stage);
+    else compress_tile<TIn, D, DP, false, FMTV, RECON>(args, cur, stage);
+    if (ns == 1 && has_next) {
       __syncthreads();
-      if (threadIdx.x == 0) mbar_arrive_expect_tx(&bar[0], tile_bytes<TIn, D>(args, n_layers, next));
+      if (threadIdx.x == 0) mbar_arrive_expect_tx(&bar[0], tile_bytes<TIn, D>(args, nt));
       __syncthreads();
-      issue_tile<TIn, D>(args, n_layers, next, smem, &bar[0]);
+      issue_tile<TIn, D>(args, nt, smem, &bar[0]);
     }
+    cur = nt;
   }
 }
 

@@ -5,7 +5,8 @@
 
 namespace nq {
 
-constexpr int kCompressThreads = 128;   // one vector per thread
+constexpr int kCompressThreads = 128;   // threads per compress / dequantize CTA
+constexpr int kCompressVecs = 64;       // vectors per compress tile (two threads per vector)
 constexpr int kMaxLayersPerLaunch = 96; // per-layer pointers travel in the kernel parameters
 
 struct LayerIO {
