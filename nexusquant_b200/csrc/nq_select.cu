@@ -2,12 +2,14 @@
 // BOS + last `sliding_window` tokens + top-n_keep of importance[1:prefix]
 // + protected positions, emitted as ascending token indices.
 //
-// One CTA per batch row.  The top-k threshold is found with an MSB-first radix
-// select over order-preserving 32-bit keys of the fp32 scores (4 passes of 8
-// bits, per-warp histograms in shared memory).  Ties at the threshold are
-// resolved toward the lower index.  The compaction is a two-pass segmented
-// scan: each thread owns a contiguous run of tokens, so the output order is
-// the token order.
+// One CTA of 1024 threads per batch row; every pass reads the row with
+// coalesced 16-byte loads (4 scores per thread per step).
+//  1. MSB-first radix select of the k-th largest order-preserving key over
+//     3 digits (11, 11, 10 bits); per-warp aggregated shared-memory histograms.
+//     After the first digit only the keys that still match the prefix count.
+//  2. Ordered compaction in chunks of 4096 tokens: a block scan of threshold ties
+//     (only in chunks that hold one) ranks them, lowest index first, and a block
+//     scan of kept counts gives each thread its output offset.
 #include "nq_common.cuh"
 #include "nq_internal.h"
 
@@ -15,9 +17,11 @@ namespace nq {
 
 constexpr int kSelThreads = 1024;
 constexpr int kSelWarps = kSelThreads / 32;
+constexpr int kSelChunk = kSelThreads * 4;
 
+// Order-preserving unsigned key; -0.0 and +0.0 compare equal (one tie class), as in a float compare.
 __device__ __forceinline__ uint32_t order_key(float f) {
-  const uint32_t u = __float_as_uint(f);
+  const uint32_t u = f == 0.0f ? 0u : __float_as_uint(f);
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
@@ -32,8 +36,9 @@ __device__ __forceinline__ bool is_protected(const int32_t* prot, int n, int t) 
   return false;
 }
 
-// Exclusive block scan of one int per thread; returns the total in *total.
-__device__ int block_exclusive_scan(int v, int* sh, int* total) {
+// Inclusive block scan of one int per thread (1024 threads); returns the inclusive value,
+// *total gets the block sum.
+__device__ __forceinline__ int block_scan_incl(int v, int* sh, int* total) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   int x = v;
 #pragma unroll
@@ -44,119 +49,155 @@ __device__ int block_exclusive_scan(int v, int* sh, int* total) {
   if (lane == 31) sh[wid] = x;
   __syncthreads();
   if (wid == 0) {
-    int s = lane < kSelWarps ? sh[lane] : 0;
+    int s = sh[lane];
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const int y = __shfl_up_sync(0xffffffffu, s, o);
       if (lane >= o) s += y;
     }
-    sh[lane] = s;  // inclusive warp totals
+    sh[lane] = s;
   }
   __syncthreads();
-  const int before = (wid > 0 ? sh[wid - 1] : 0) + x - v;
+  const int r = x + (wid > 0 ? sh[wid - 1] : 0);
   *total = sh[kSelWarps - 1];
   __syncthreads();
-  return before;
+  return r;
+}
+
+__device__ __forceinline__ float4 load4(const float* x, int t0, int n) {
+  if (t0 + 3 < n && ((reinterpret_cast<uintptr_t>(x + t0) & 15) == 0)) return *reinterpret_cast<const float4*>(x + t0);
+  float4 r;
+  r.x = t0 < n ? x[t0] : 0.0f;
+  r.y = t0 + 1 < n ? x[t0 + 1] : 0.0f;
+  r.z = t0 + 2 < n ? x[t0 + 2] : 0.0f;
+  r.w = t0 + 3 < n ? x[t0 + 3] : 0.0f;
+  return r;
 }
 
 __global__ void __launch_bounds__(kSelThreads) select_kernel(const float* imp, int seq, int sw, int n_keep,
                                                              const int32_t* prot, int n_prot, int32_t* kept_idx,
                                                              int32_t* kept_count) {
-  __shared__ uint32_t hist[kSelWarps][256];
-  __shared__ uint32_t tot[256];
+  __shared__ uint32_t hist[2048];
   __shared__ uint32_t s_pref, s_rem;
   __shared__ int scan_sh[32];
   const int b = blockIdx.x;
   const float* x = imp + (int64_t)b * seq;
   const int prefix = max(seq - sw, 0);
   const int k = (prefix > 1 && n_keep > 0) ? min(n_keep, prefix - 1) : 0;
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
 
-  // ---- radix select: threshold key of the k-th largest score in [1, prefix)
-  uint32_t pref = 0, mask = 0;
-  uint32_t rem = (uint32_t)k;
+  // ---- radix select over digits [31:21], [20:10], [9:0]
+  uint32_t pref = 0, mask = 0, rem = (uint32_t)k;
   if (k > 0) {
-    for (int shift = 24; shift >= 0; shift -= 8) {
-      for (int i = threadIdx.x; i < kSelWarps * 256; i += kSelThreads) (&hist[0][0])[i] = 0u;
+    const int shifts[3] = {21, 10, 0};
+    const int bits[3] = {11, 11, 10};
+    for (int p = 0; p < 3; ++p) {
+      const int sh = shifts[p], nb = 1 << bits[p];
+      for (int i = threadIdx.x; i < nb; i += kSelThreads) hist[i] = 0u;
       __syncthreads();
-      for (int t0 = 1; t0 < prefix; t0 += kSelThreads) {
-        const int t = t0 + threadIdx.x;
-        bool act = false;
-        uint32_t dig = 0;
-        if (t < prefix) {
-          const uint32_t key = order_key(x[t]);
-          if ((key & mask) == pref) { act = true; dig = (key >> shift) & 0xFFu; }
-        }
-        const uint32_t am = __ballot_sync(0xffffffffu, act);
-        if (act) {
-          const uint32_t peers = __match_any_sync(am, dig);
-          if ((__ffs(peers) - 1) == lane) hist[wid][dig] += __popc(peers);
+      for (int c0 = 0; c0 < prefix; c0 += kSelChunk) {
+        const int t0 = c0 + threadIdx.x * 4;
+        const float4 v4 = load4(x, t0, prefix);
+        const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int t = t0 + u;
+          const uint32_t key = order_key(vv[u]);
+          const bool act = t >= 1 && t < prefix && (key & mask) == pref;
+          const uint32_t dig = (key >> sh) & (uint32_t)(nb - 1);
+          const uint32_t am = __ballot_sync(0xffffffffu, act);
+          if (act) {
+            const uint32_t peers = __match_any_sync(am, dig);
+            if ((__ffs(peers) - 1) == lane) atomicAdd(&hist[dig], (uint32_t)__popc(peers));
+          }
         }
       }
       __syncthreads();
-      if (threadIdx.x < 256) {
-        uint32_t s = 0;
-        for (int w = 0; w < kSelWarps; ++w) s += hist[w][threadIdx.x];
-        tot[threadIdx.x] = s;
-      }
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        uint32_t above = 0;
-        int d = 255;
-        for (; d > 0; --d) {
-          if (above + tot[d] >= rem) break;
-          above += tot[d];
+      if (threadIdx.x < 32) {
+        // warp 0: find the digit holding the rem-th largest key (scan bins from the top)
+        const int per = nb / 32;
+        uint32_t cnt = 0;
+        const int hi0 = nb - 1 - lane * per;  // this lane's bins: hi0 down to hi0 - per + 1
+        for (int i = 0; i < per; ++i) cnt += hist[hi0 - i];
+        // exclusive prefix of counts over lanes (lane 0 = highest bins)
+        uint32_t inc = cnt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const uint32_t y = __shfl_up_sync(0xffffffffu, inc, o);
+          if (lane >= o) inc += y;
         }
-        s_pref = pref | ((uint32_t)d << shift);
-        s_rem = rem - above;
+        const uint32_t exc = inc - cnt;
+        if (exc < rem && rem <= inc) {
+          uint32_t above = exc;
+          int d = hi0;
+          for (int i = 0; i < per; ++i, --d) {
+            const uint32_t hcount = hist[d];
+            if (above + hcount >= rem) break;
+            above += hcount;
+          }
+          s_pref = pref | ((uint32_t)d << sh);
+          s_rem = rem - above;
+        }
       }
       __syncthreads();
       pref = s_pref;
       rem = s_rem;
-      mask |= 0xFFu << shift;
+      mask |= (uint32_t)(nb - 1) << sh;
       __syncthreads();
     }
   }
-  const uint32_t thr = pref;   // exact key of the k-th largest
-  const int need_eq = (int)rem; // how many threshold-equal scores to keep (lowest index first)
+  const uint32_t thr = pref;    // exact key of the k-th largest prefix score
+  const int need_eq = (int)rem; // threshold-equal scores to keep, lowest index first
 
-  // ---- compaction over contiguous per-thread runs
-  const int per = (seq + kSelThreads - 1) / kSelThreads;
-  const int t_begin = min(seq, threadIdx.x * per), t_end = min(seq, t_begin + per);
-  int n_eq = 0;
-  if (k > 0)
-    for (int t = max(t_begin, 1); t < min(t_end, prefix); ++t) n_eq += (order_key(x[t]) == thr);
-  int eq_total;
-  const int eq_before = block_exclusive_scan(n_eq, scan_sh, &eq_total);
-  // pass A: count kept tokens of this run
-  auto keep_at = [&](int t, int& eq_rank) -> bool {
-    bool keep = (t == 0) || (sw > 0 && t >= seq - sw);
-    if (!keep && k > 0 && t >= 1 && t < prefix) {
-      const uint32_t key = order_key(x[t]);
-      if (key > thr) keep = true;
-      else if (key == thr) { keep = eq_rank < need_eq; ++eq_rank; }
-    } else if (k > 0 && t >= 1 && t < prefix && order_key(x[t]) == thr) {
-      ++eq_rank;
+  // ---- ordered compaction, 4096 tokens per chunk
+  int out_base = 0, eq_base = 0;
+  int32_t* dst = kept_idx + (int64_t)b * seq;
+  for (int c0 = 0; c0 < seq; c0 += kSelChunk) {
+    const int t0 = c0 + threadIdx.x * 4;
+    const float4 v4 = load4(x, t0, seq);
+    const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
+    // keep[u]: BOS, window, above threshold or protected; tie[u]: equal to the threshold key
+    bool keep[4], tie[4];
+    int n_tie_l = 0;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int t = t0 + u;
+      bool kp = false, eq = false;
+      if (t < seq) {
+        if (t == 0 || (sw > 0 && t >= seq - sw)) {
+          kp = true;
+        } else if (k > 0 && t < prefix) {
+          const uint32_t key = order_key(vv[u]);
+          kp = key > thr;
+          eq = key == thr;
+        }
+        if (!kp && n_prot > 0) kp = is_protected(prot, n_prot, t);
+      }
+      keep[u] = kp;
+      tie[u] = eq;
+      n_tie_l += eq;
     }
-    if (!keep && n_prot > 0) keep = is_protected(prot, n_prot, t);
-    return keep;
-  };
-  int cnt = 0;
-  {
-    int er = eq_before;
-    for (int t = t_begin; t < t_end; ++t) cnt += keep_at(t, er) ? 1 : 0;
+    // Tie ranks: only the first need_eq threshold ties of the row (lowest index) are top-k members.
+    // A __syncthreads_or keeps the common no-tie chunks to a single barrier.
+    if (__syncthreads_or(n_tie_l)) {
+      int chunk_ties;
+      int r = eq_base + block_scan_incl(n_tie_l, scan_sh, &chunk_ties) - n_tie_l;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (tie[u]) keep[u] = keep[u] || r < need_eq;
+        r += tie[u];
+      }
+      eq_base += chunk_ties;
+    }
+    const int n_out_l = (int)keep[0] + (int)keep[1] + (int)keep[2] + (int)keep[3];
+    int chunk_out;
+    int o = out_base + block_scan_incl(n_out_l, scan_sh, &chunk_out) - n_out_l;
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (keep[u]) dst[o++] = t0 + u;
+    out_base += chunk_out;
   }
-  int total;
-  const int out_before = block_exclusive_scan(cnt, scan_sh, &total);
-  {
-    int er = eq_before;
-    int o = out_before;
-    int32_t* dst = kept_idx + (int64_t)b * seq;
-    for (int t = t_begin; t < t_end; ++t)
-      if (keep_at(t, er)) dst[o++] = t;
-  }
-  if (threadIdx.x == 0) kept_count[b] = total;
-  (void)eq_total;
+  if (threadIdx.x == 0) kept_count[b] = out_base;
 }
 
 size_t select_workspace_bytes(int, int) { return 0; }

@@ -253,6 +253,33 @@ def test_select_large(orc, T, sw, rate):
     _check_select(orc, imp, T, sw, rate)
 
 
+@pytest.mark.parametrize("case", ["all_equal", "few_values", "negative", "protected_ties", "ragged_batch"])
+def test_select_adversarial(orc, case):
+    rng = np.random.default_rng(7)
+    prot = None
+    if case == "all_equal":
+        T, sw, rate = 9001, 16, 0.5
+        imp = np.full((1, T), 0.25, np.float32)
+    elif case == "few_values":
+        T, sw, rate = 20000, 32, 0.3
+        imp = rng.integers(0, 5, (2, T)).astype(np.float32)
+    elif case == "negative":
+        T, sw, rate = 12345, 7, 0.6
+        imp = (rng.standard_normal((1, T)) * 1e-3).astype(np.float32)
+        imp[0, ::97] = -0.0
+        imp[0, 1::97] = 0.0
+    elif case == "protected_ties":
+        T, sw, rate = 10000, 32, 0.5
+        imp = rng.integers(0, 3, (1, T)).astype(np.float32)
+        prot = list(range(0, T, 37))
+    else:
+        T, sw, rate = 4099, 3, 0.45
+        imp = rng.random((3, T)).astype(np.float32)
+        imp[1] = np.round(imp[1] * 8) / 8
+        prot = [5, 4098, 2000]
+    _check_select(orc, imp, T, sw, rate, prot)
+
+
 def test_gather_and_delta(orc):
     cfg = syn.CacheConfig("t", 1, 1, 2, 30, 128)
     k, v = syn.cpu_layer(cfg, 3)
