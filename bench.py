@@ -460,11 +460,14 @@ def main():
     achieved = algo / (kms / 1e3) / 1e9 if sh.quant else 0.0
     dq_bytes = algo  # dequantize moves the same bytes in the other direction
     dq_achieved = dq_bytes / (dms / 1e3) / 1e9 if sh.quant else 0.0
+    # DRAM bytes (read + write) per algorithmic byte of the compress kernel, from one ncu capture
+    # (profiles/traffic.json); traffic of this launch = that ratio x this launch's algorithmic bytes.
     traffic = None
     try:
         with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
-            traffic = json.load(f).get(cfg.name, {}).get(f"compress_world{world}")
-    except Exception:
+            ratio = json.load(f)["compress_kernel"]["dram_bytes_per_algo_byte"]
+        traffic = int(round(ratio * algo)) if sh.quant else None
+    except (OSError, KeyError, ValueError):
         pass
 
     e2e, e2e_err = (None, "disabled")
@@ -485,7 +488,7 @@ def main():
                        "seq": cfg.seq, "head_dim": cfg.head_dim, "key_bits": cfg.key_bits,
                        "value_bits": cfg.value_bits, "eviction_rate": cfg.eviction_rate,
                        "kept_tokens": sh.cap, "protected_layers": sorted(sh.protected),
-                       "parallelism": f"layer-sharded x{world}", "l2": "inputs (42.95 GB) larger than L2; no flush"},
+                       "parallelism": f"layer-sharded x{world}", "l2": f"inputs ({cfg.fp16_bytes / 1e9:.2f} GB) larger than L2; no flush"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
                          "kernel": "compress_kernel", "launch_ms": round(kms, 4), "algo_bytes": algo},
