@@ -34,6 +34,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 from nexusquant_b200 import kernels as K  # noqa: E402
+from nexusquant_b200 import sharding as S  # noqa: E402
 from nexusquant_b200 import synthetic as syn  # noqa: E402
 from nexusquant_b200.pipeline import kept_capacity, n_keep_for  # noqa: E402
 
@@ -104,36 +105,20 @@ class ClockSampler:
                 "reasons": [n for b, n in self.REASONS.items() if self.reasons & b]}
 
 
-# -------------------------------------------------------------------------- plan
-def assign_layers(n_layers: int, protected: set, world: int):
-    """Cost-balanced layer -> rank assignment (protected layers cost ~1.6x a quantized one:
-    they move 2 x 2 x d bytes per kept row instead of 2 x d + packed bytes)."""
-    cost = {l: (1.6 if l in protected else 1.0) for l in range(n_layers)}
-    order = sorted(range(n_layers), key=lambda l: (-cost[l], l))
-    load = [0.0] * world
-    owned = [[] for _ in range(world)]
-    for l in order:
-        r = min(range(world), key=lambda i: (load[i], i))
-        owned[r].append(l)
-        load[r] += cost[l]
-    return [sorted(o) for o in owned]
-
-
+# -------------------------------------------------------------------------- shard
 class Shard:
     """One rank's part of the compression of a config-4-shaped cache."""
 
     def __init__(self, cfg, rank: int, world: int, device, group=None):
         self.cfg, self.rank, self.world, self.dev, self.group = cfg, rank, world, device, group
         L = cfg.n_layers
-        pb = cfg.protect_boundary
-        self.protected = set(range(pb)) | set(range(L - pb, L)) if pb else set()
-        self.owned = assign_layers(L, self.protected, world)[rank]
-        self.quant = [l for l in self.owned if l not in self.protected]
-        self.prot = [l for l in self.owned if l in self.protected]
+        self.plan = S.make_plan(L, cfg.heads, cfg.protect_boundary, rank, world)
+        self.owned = list(self.plan.layers)
+        self.quant = list(self.plan.quantized)
+        self.prot = list(self.plan.protected)
+        self.protected = S.protected_layers(L, cfg.protect_boundary)
         h = cfg.heads
-        per = math.ceil(h / world)
-        self.h0, self.h1 = min(h, rank * per), min(h, (rank + 1) * per)
-        self.per = per
+        self.h0, self.h1, self.per = self.plan.head_begin, self.plan.head_end, self.plan.heads_per_rank
         self.nk = n_keep_for(cfg.seq, cfg.sliding_window, cfg.eviction_rate)
         self.cap = kept_capacity(cfg.seq, cfg.sliding_window, self.nk)
         # resident data: this rank's layers, plus layer 0's keys for scoring
@@ -152,14 +137,11 @@ class Shard:
             torch.empty((b, h, n), dtype=torch.float16, device=device), *self.levels) for _ in self.quant]
         self.prot_out = {l: (torch.empty((b, h, n, d), dtype=torch.float16, device=device),
                              torch.empty((b, h, n, d), dtype=torch.float16, device=device)) for l in self.prot}
-        self.gathered = torch.empty((world * b * per, T), dtype=torch.float32, device=device)
-        sizes = [0] * L
-        for l in self.quant:
-            sizes[l] = b * h * n * (K.packed_bytes(dp, self.levels[0]) + K.packed_bytes(dp, self.levels[1]) + 4)
-        for l in self.prot:
-            sizes[l] = 2 * b * h * n * d * 2
-        self.sizes = torch.tensor(sizes, dtype=torch.int64, device=device)
-        self.sizes_all = torch.zeros((world, L), dtype=torch.int64, device=device)
+        self.gathered = torch.empty((world * b * self.per, T), dtype=torch.float32, device=device)
+        pkv = K.packed_bytes(dp, self.levels[0]) + K.packed_bytes(dp, self.levels[1]) + 4
+        self.sizes = S.local_layer_sizes(self.plan, [b * h * n * pkv] * len(self.quant),
+                                         [2 * b * h * n * d * 2] * len(self.prot), device=device)
+        self.sizes_all = torch.zeros((world * L,), dtype=torch.int64, device=device)
         self.launches = 0
 
     # bytes
@@ -183,13 +165,7 @@ class Shard:
             self.launches += 3
         else:
             ph = torch.zeros((b, 0, T), dtype=torch.float32, device=self.dev)
-        if self.world > 1:
-            buf = torch.zeros((b, self.per, T), dtype=torch.float32, device=self.dev)
-            buf[:, :ph.shape[1]] = ph
-            dist.all_gather_into_tensor(self.gathered, buf.reshape(b * self.per, T), group=self.group)
-            allh = self.gathered.reshape(self.world, b, self.per, T).transpose(0, 1).reshape(b, -1, T)[:, :h]
-        else:
-            allh = ph
+        allh = S.gather_head_scores(ph, self.plan, self.group, self.gathered)
         imp = K.reduce_heads(allh, float(h))
         idx, cnt = K.select_keep(imp, cfg.sliding_window, self.nk)
         self.launches += 2
@@ -206,7 +182,7 @@ class Shard:
         self.kept_idx, self.kept_count = idx, cnt
         if self.world > 1:
             # global index of the compressed cache: per-layer byte sizes from every rank
-            dist.all_gather_into_tensor(self.sizes_all, self.sizes, group=self.group)
+            S.gather_layer_index(self.sizes, self.plan, self.group, self.sizes_all)
 
     def compress_only(self):
         K.compress_layers([self.K[l] for l in self.quant], [self.V[l] for l in self.quant],
