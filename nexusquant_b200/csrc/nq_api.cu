@@ -59,7 +59,7 @@ nq_status_t nq_compress_layers(const nq_compress_params_t* p, nq_stream_t stream
   if (p->kept_idx == nullptr && p->n_kept > p->seq) return NQ_ERR_INVALID_ARG;
   if (p->n_layers == 0 || p->batch == 0 || p->heads == 0 || p->n_kept == 0) return NQ_OK;
   const int eb = elem_bytes(p->in_dtype);
-  // TMA bulk copies need 16-byte aligned rows
+  // 16-byte cp.async copies need 16-byte aligned rows
   if ((p->in_stride_b * eb) % 16 || (p->in_stride_h * eb) % 16 || (p->in_stride_t * eb) % 16) return NQ_ERR_ALIGNMENT;
   if ((p->out_stride_b * 2) % 16 || (p->out_stride_h * 2) % 16 || (p->out_stride_t * 2) % 16) return NQ_ERR_ALIGNMENT;
   bool any_key = false, any_out = false;

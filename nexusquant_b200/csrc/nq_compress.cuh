@@ -1,7 +1,7 @@
 // Fused KV compress kernel (sm_100a).
 //
 // Per vector (one (layer, K|V, batch, head, kept token) row of d values):
-//   TMA bulk copy row -> shared -> fp32 -> [keys] inverse split-half RoPE at the
+//   cp.async row -> shared -> fp32 -> [keys] inverse split-half RoPE at the
 //   source position -> zero pad to d_p -> Walsh-Hadamard butterfly in registers
 //   -> * fl32(1/sqrt(d_p)) -> amax, sc = amax / (L/2) -> x / sc (correctly
 //   rounded) -> relaxed-E8 nearest point per 8-group -> clamp -> packed codes,
@@ -21,8 +21,9 @@
 //  * K vs V and the packing format are template parameters, so the per-vector
 //    code is one branch-free basic block.
 //  * Persistent CTAs walk the tile list; each has a two-stage shared-memory
-//    pipeline: while tile i is computed, the rows of tile i+1 are in flight
-//    through the TMA engine (cp.async.bulk, no multicast).
+//    pipeline: while tile i is computed, the rows of tile i+1 are in flight as
+//    16-byte cp.async copies (per-lane operands: no per-row issue loop, and a
+//    warp barrier suffices because each warp copies the rows it computes).
 //  * A tile is HG heads x (64/HG) tokens of one (layer, K|V, batch); threads of
 //    a warp that share a token read the same RoPE row (shared-memory broadcast).
 #include "nq_common.cuh"
@@ -38,82 +39,140 @@ struct Fmt {
   static constexpr int kWords = kBytes / 4;
 };
 
-// Relaxed-E8 choice for one 8-group (nexusquant/core/e8_lattice.py:27-69), from
-// the per-coordinate gaps e = x - round(x) and the bit patterns of x + M and
-// fl(x - 0.5) + M (M = 1.5 * 2^23, whose low bits hold the rounded integers).
-// Emits fields f = code + 8 with code = 2 * lattice point clamped to [-L, L].
-// B is chosen iff sum_i |e_i| + odd * (1 - 2 min_i |e_i|) > 2 (fp32, pairwise sum):
-// the same arithmetic as the CPU oracle.
-__device__ __forceinline__ void e8_fields(const float (&e)[8], const uint32_t (&sb)[8], const uint32_t (&bb)[8],
-                                          int levels, int (&f)[8]) {
-  // pairwise sum ((g0+g1)+(g2+g3))+((g4+g5)+(g6+g7)): depth 3 instead of 7
-  float g[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) g[i] = fabsf(e[i]);
-  const float gsum = __fadd_rn(__fadd_rn(__fadd_rn(g[0], g[1]), __fadd_rn(g[2], g[3])),
-                               __fadd_rn(__fadd_rn(g[4], g[5]), __fadd_rn(g[6], g[7])));
-  // tournament argmin keeping the left entry on ties = first index of the minimum
-  float tg[4], te[4];
-  int ti[4];
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const bool r = g[2 * k + 1] < g[2 * k];
-    tg[k] = r ? g[2 * k + 1] : g[2 * k];
-    te[k] = r ? e[2 * k + 1] : e[2 * k];
-    ti[k] = r ? 2 * k + 1 : 2 * k;
+// Packed-field layout of one 8-group.  Field i sits at bit sh(i) of word wd(i); an
+// A field is f = 2a + BIAS and a B field f = 2k + 1 + BIAS, with a = rint(x) and
+// k = rint(x - 1/2), so code = 2 * lattice point = f - BIAS.  Formats 0 and 1 keep
+// f (nibbles / 5-bit fields, BIAS 8); format 2 turns f into the signed code byte.
+template <int FMT>
+struct GF {
+  static constexpr int kWords = FMT == 0 ? 1 : 2;
+  static constexpr int kBias = FMT == 2 ? 32 : 8;
+  static constexpr int kWidth = FMT == 0 ? 4 : (FMT == 1 ? 5 : 8);
+  static constexpr int kPer = FMT == 0 ? 8 : 4;  // fields per word
+  static constexpr uint32_t kMask = (1u << kWidth) - 1u;
+  __host__ __device__ static constexpr int sh(int i) { return kWidth * (i % kPer); }
+  __host__ __device__ static constexpr int wd(int i) { return i / kPer; }
+  // c replicated into every field of a word (mod 2^32)
+  __host__ __device__ static constexpr uint32_t rep(uint32_t c) {
+    uint32_t r = 0;
+    for (int i = 0; i < kPer; ++i) r += c << (kWidth * i);
+    return r;
   }
+  static constexpr uint32_t kBit0 = rep(1u), kBit1 = rep(2u);
+  // Accumulator seeds: sum_i bits(x_i + M) * 2^(sh(i)+1) + seed = sum_i field_i << sh(i),
+  // because bits(x + M) = kMagicBits + round(x) and the magic part cancels mod 2^32.
+  static constexpr uint32_t kSeedA = rep((uint32_t)kBias) - rep(2u * kMagicBits);
+  static constexpr uint32_t kSeedB = rep((uint32_t)kBias + 1u) - rep(2u * kMagicBits);
+};
+
+__device__ __forceinline__ uint32_t umin(uint32_t a, uint32_t b) { return a < b ? a : b; }
+
+// Relaxed-E8 nearest point of one 8-group (nexusquant/core/e8_lattice.py:27-69), packed.
+//
+// Inputs per coordinate: e = x - round(x), sa = bits(x + M), sb = bits(fl(x - 1/2) + M)
+// (M = 1.5 * 2^23).  Decision, as in the CPU oracle: B iff
+//   sum_i |e_i| (pairwise) + odd * (1 - 2 min_i |e_i|) > 2,
+// and for A with an odd coordinate sum the first coordinate of smallest |e| moves one step
+// toward x.  Everything after the gaps runs on the packed words:
+//  * the A and B fields of the whole group are accumulated with one IMAD per coordinate;
+//  * parity = popcount of the A fields' bit 1;
+//  * argmin: unsigned minima of (bits(|e_i|) << 2 | i mod 4) per half (first index on
+//    ties), then the halves compared on |e|;
+//  * the step's direction is fB - fA at that coordinate (+1 when e = 0);
+//  * clamping to [-L, L]: with L a power of two, sc = amax * 2/L is exact and |x| <= L/2,
+//    so a field leaves the range only as B at x = +L/2 (L >= 4, f = L + 9 + BIAS - 8),
+//    B at x = -L/2 (L = 2, f = 5), or the A step at a = +L/2 -- each is patched directly.
+template <int FMT>
+__device__ __forceinline__ void e8_group(const float (&e)[8], const uint32_t (&sa)[8], const uint32_t (&sb)[8],
+                                         int levels, uint32_t (&w)[GF<FMT>::kWords]) {
+  using F = GF<FMT>;
+  constexpr int NW = F::kWords;
+  const float gsum = __fadd_rn(__fadd_rn(__fadd_rn(fabsf(e[0]), fabsf(e[1])), __fadd_rn(fabsf(e[2]), fabsf(e[3]))),
+                               __fadd_rn(__fadd_rn(fabsf(e[4]), fabsf(e[5])), __fadd_rn(fabsf(e[6]), fabsf(e[7]))));
+  uint32_t key[8];
 #pragma unroll
-  for (int k = 0; k < 2; ++k) {
-    const bool r = tg[2 * k + 1] < tg[2 * k];
-    tg[k] = r ? tg[2 * k + 1] : tg[2 * k];
-    te[k] = r ? te[2 * k + 1] : te[2 * k];
-    ti[k] = r ? ti[2 * k + 1] : ti[2 * k];
-  }
-  const bool r = tg[1] < tg[0];
-  const float gmin = r ? tg[1] : tg[0];
-  const float emin = r ? te[1] : te[0];
-  const int idx = r ? ti[1] : ti[0];
-  const uint32_t par = (sb[0] ^ sb[1] ^ sb[2] ^ sb[3] ^ sb[4] ^ sb[5] ^ sb[6] ^ sb[7]) & 1u;
-  const float lhs = par ? __fadd_rn(gsum, __fsub_rn(1.0f, __fmul_rn(2.0f, gmin))) : gsum;
-  const bool use_b = lhs > 2.0f;
-  // field = 2 * round + 8 (A) or 2 * round(x - 0.5) + 9 (B); the magic offset cancels mod 2^32
-  const uint32_t off = (use_b ? 9u : 8u) - 2u * kMagicBits;
-  const int fix = (par && !use_b) ? (emin >= 0.0f ? 2 : -2) : 0;
-  const int lo = 8 - levels, hi = 8 + levels;
+  for (int i = 0; i < 8; ++i) key[i] = (__float_as_uint(e[i]) << 2) | (uint32_t)(i & 3);  // |e| <= 1/2: bit 30 is 0
+  const uint32_t kl = umin(umin(key[0], key[1]), umin(key[2], key[3]));
+  const uint32_t kh = umin(umin(key[4], key[5]), umin(key[6], key[7]));
+  const bool in_hi = (kh >> 2) < (kl >> 2);
+  const uint32_t km = in_hi ? kh : kl;
+  const uint32_t gbits = km >> 2;
+  const int idx = (in_hi ? 4 : 0) + (int)(km & 3u);
+
+  uint32_t wa[NW], wb[NW];
+#pragma unroll
+  for (int k = 0; k < NW; ++k) { wa[k] = F::kSeedA; wb[k] = F::kSeedB; }
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    const uint32_t base = use_b ? bb[i] : sb[i];
-    int v = static_cast<int>(2u * base + off);
-    v += (i == idx) ? fix : 0;
-    f[i] = min(max(v, lo), hi);
+    wa[F::wd(i)] += sa[i] * (2u << F::sh(i));
+    wb[F::wd(i)] += sb[i] * (2u << F::sh(i));
+  }
+  uint32_t par;
+  if constexpr (NW == 1) par = __popc(wa[0] & F::kBit1) & 1u;
+  else par = __popc((wa[0] ^ wa[1]) & F::kBit1) & 1u;
+  const float lhs = par ? __fadd_rn(gsum, __fmaf_rn(-2.0f, __uint_as_float(gbits), 1.0f)) : gsum;
+  const bool use_b = lhs > 2.0f;
+
+  // A step at coordinate idx
+  const int sh = F::kWidth * (FMT == 0 ? idx : (idx & 3));
+  const uint32_t wa_i = (NW == 1 || idx < 4) ? wa[0] : wa[NW - 1];
+  const uint32_t wb_i = (NW == 1 || idx < 4) ? wb[0] : wb[NW - 1];
+  const int fa = (int)((wa_i >> sh) & F::kMask), fb = (int)((wb_i >> sh) & F::kMask);
+  const int d = gbits == 0u ? 2 : 2 * (fb - fa);
+  const bool step = par && !use_b && !(d > 0 && fa == F::kBias + levels);
+  const uint32_t delta = step ? ((uint32_t)d << sh) : 0u;
+
+  // B clamps
+#pragma unroll
+  for (int k = 0; k < NW; ++k) {
+    const uint32_t x = wb[k];
+    if constexpr (FMT == 0) {
+      if (levels == 4) wb[k] = x - (x & (x >> 2) & (x >> 3) & F::kBit0);   // 13 -> 12
+      else wb[k] = x + (x & (x >> 2) & ~(x >> 1) & F::kBit0);            // L = 2: 5 -> 6
+    } else if constexpr (FMT == 1) {
+      wb[k] = x - (x & (x >> 4) & F::kBit0);                              // 17 -> 16
+    } else {
+      wb[k] = x - (x & (x >> 4) & (x >> 5) & F::kBit0);                   // 49 -> 48
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < NW; ++k) {
+    const bool mine = NW == 1 || ((idx >> 2) == k);
+    uint32_t v = use_b ? wb[k] : wa[k] + (mine ? delta : 0u);
+    if constexpr (FMT == 2) {
+      // f = c + 32 in [16, 48] -> signed code byte: f ^ 32 is c for c >= 0 and c + 64 for
+      // c < 0, which then needs 0xC0 on top
+      const uint32_t y = v ^ 0x20202020u;
+      v = y + (y & 0x20202020u) * 6u;
+    }
+    w[k] = v;
   }
 }
 
-template <int FMT, int DP>
-__device__ __forceinline__ void pack_fields(uint32_t* w, int g, const int (&f)[8]) {
+// Place a group's packed words into the row words of its region.
+template <int FMT>
+__device__ __forceinline__ void place_group(uint32_t* r, int g, const uint32_t (&w)[GF<FMT>::kWords]) {
   if constexpr (FMT == 0) {
-    uint32_t v = 0;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) v |= static_cast<uint32_t>(f[i]) << (4 * i);
-    w[g] = v;
+    r[g] = w[0];
   } else if constexpr (FMT == 1) {
-    uint64_t v = 0;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) v |= static_cast<uint64_t>(f[i]) << (5 * i);
+    const uint64_t v = (uint64_t)w[0] | ((uint64_t)w[1] << 20);
     const int bit = 40 * g;
     const int wi = bit >> 5, sh = bit & 31;  // sh is 0, 8, 16 or 24
-    w[wi] |= static_cast<uint32_t>(v << sh);
-    w[wi + 1] |= static_cast<uint32_t>(v >> (32 - sh));
+    r[wi] |= static_cast<uint32_t>(v << sh);
+    r[wi + 1] |= static_cast<uint32_t>(v >> (32 - sh));
   } else {
-    uint32_t lo = 0, hi = 0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      lo |= (static_cast<uint32_t>(f[i] - 8) & 0xFFu) << (8 * i);
-      hi |= (static_cast<uint32_t>(f[4 + i] - 8) & 0xFFu) << (8 * i);
-    }
-    w[2 * g] = lo;
-    w[2 * g + 1] = hi;
+    r[2 * g] = w[0];
+    r[2 * g + 1] = w[1];
   }
+}
+
+// Code (2 * lattice point) of coordinate i from a group's packed words.
+template <int FMT>
+__device__ __forceinline__ int group_code(const uint32_t (&w)[GF<FMT>::kWords], int i) {
+  using F = GF<FMT>;
+  const uint32_t f = (w[F::wd(i)] >> F::sh(i)) & F::kMask;
+  if constexpr (FMT == 2) return (int)(int8_t)f;
+  else return (int)f - 8;
 }
 
 
@@ -229,45 +288,49 @@ struct Smem {
   }
 };
 
-// Issue the TMA copies of one tile into a stage (thread 2v copies row v; thread 0 posts the bytes first).
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Copy one tile's rows (and, for keys, its tokens' RoPE rows) into a stage with 16-byte
+// cp.async: the two threads of vector v copy alternate chunks of row v, and the 2*HG
+// threads of a token share its cos / sin rows.  Every region of the stage is written and
+// read by lanes of one warp, so a warp barrier orders the copies and their readers.
 template <typename TIn, int D>
-__device__ __forceinline__ void issue_tile(const CompressArgs& a, const Tile& t, uint8_t* stage, uint64_t* bar) {
+__device__ __forceinline__ void issue_tile(const CompressArgs& a, const Tile& t, uint8_t* stage) {
   using S = Smem<TIn, D>;
-  if (threadIdx.x & 1) return;
   const LayerIO& L = a.layers[t.layer];
   const bool key = t.kv == 0;
   const TIn* src = static_cast<const TIn*>(key ? L.k : L.v);
   const int HG = a.head_group, TOK = kCompressVecs / HG;
   const int count = a.kept_count ? min(a.kept_count[t.b], a.n_kept) : a.n_kept;
-  const int v = threadIdx.x >> 1;
+  const int v = threadIdx.x >> 1, h = threadIdx.x & 1;
   const int tok_l = v / HG, head_l = v % HG;
   const int j = t.tt * TOK + tok_l;
   const int head = t.hg * HG + head_l;
-  if (src != nullptr && j < count && head < a.heads) {
-    const int row = a.kept_idx ? a.kept_idx[(int64_t)t.b * a.n_kept + j] : j;
-    const TIn* g = src + (int64_t)t.b * a.in_stride_b + (int64_t)head * a.in_stride_h + (int64_t)row * a.in_stride_t;
-    bulk_g2s(stage + v * S::kRowStride, g, S::kRowBytes, bar);
-    if (key && head_l == 0) {
-      const int pos = a.positions ? a.positions[(int64_t)t.b * a.n_kept + j] : row;
-      uint8_t* trow = stage + S::kRows + tok_l * S::kTabStride;
-      bulk_g2s(trow, a.rope_cos + (int64_t)pos * (D / 2), (D / 2) * 4, bar);
-      bulk_g2s(trow + (D / 2) * 4, a.rope_sin + (int64_t)pos * (D / 2), (D / 2) * 4, bar);
+  if (src == nullptr || j >= count) return;
+  const int row = a.kept_idx ? a.kept_idx[(int64_t)t.b * a.n_kept + j] : j;
+  if (key) {
+    // every lane of the token's group copies, whether or not its own head exists
+    constexpr int HALF = (D / 2) * 4 / 16;  // chunks of one cos (or sin) row
+    const int pos = a.positions ? a.positions[(int64_t)t.b * a.n_kept + j] : row;
+    uint8_t* trow = stage + S::kRows + tok_l * S::kTabStride;
+    const float* cs = a.rope_cos + (int64_t)pos * (D / 2);
+    const float* sn = a.rope_sin + (int64_t)pos * (D / 2);
+    for (int c = 2 * head_l + h; c < 2 * HALF; c += 2 * HG) {
+      if (c < HALF) cp_async16(trow + 16 * c, cs + 4 * c);
+      else cp_async16(trow + 16 * c, sn + 4 * (c - HALF));
     }
   }
-}
-
-template <typename TIn, int D>
-__device__ __forceinline__ uint32_t tile_bytes(const CompressArgs& a, const Tile& t) {
-  const LayerIO& L = a.layers[t.layer];
-  const bool key = t.kv == 0;
-  if ((key ? L.k : L.v) == nullptr) return 0;
-  const int HG = a.head_group, TOK = kCompressVecs / HG;
-  const int count = a.kept_count ? min(a.kept_count[t.b], a.n_kept) : a.n_kept;
-  const int toks = max(0, min(TOK, count - t.tt * TOK));
-  const int heads = min(HG, a.heads - t.hg * HG);
-  uint32_t bytes = (uint32_t)(toks * heads) * Smem<TIn, D>::kRowBytes;
-  if (key) bytes += (uint32_t)toks * (D / 2) * 8;
-  return bytes;
+  if (head >= a.heads) return;
+  const uint8_t* g = reinterpret_cast<const uint8_t*>(src + (int64_t)t.b * a.in_stride_b +
+                                                      (int64_t)head * a.in_stride_h + (int64_t)row * a.in_stride_t);
+  uint8_t* dst = stage + v * S::kRowStride;
+#pragma unroll
+  for (int c = h; c < S::kRowBytes / 16; c += 2) cp_async16(dst + 16 * c, g + 16 * c);
 }
 
 // --------------------------------------------------------------------------
@@ -404,7 +467,7 @@ __device__ __forceinline__ void compress_tile(const CompressArgs& a, const Tile&
   uint32_t wl[RW], wh[RW];
 #pragma unroll
   for (int i = 0; i < RW; ++i) { wl[i] = 0u; wh[i] = 0u; }
-  int fl_all[RECON ? HP : 1][8], fh_all[RECON ? HP : 1][8];
+  uint32_t gl_all[RECON ? GT : 1][GF<FMT>::kWords], gh_all[RECON ? GT : 1][GF<FMT>::kWords];
 #pragma unroll
   for (int g = 0; g < GT; ++g) {
     float elo[8], ehi[8];
@@ -426,14 +489,14 @@ __device__ __forceinline__ void compress_tile(const CompressArgs& a, const Tile&
       slo[i] = __float_as_uint(s0); shi[i] = __float_as_uint(s1);
       blo[i] = __float_as_uint(b0); bhi[i] = __float_as_uint(b1);
     }
-    int flo[8], fhi[8];
-    e8_fields(elo, slo, blo, levels, flo);
-    e8_fields(ehi, shi, bhi, levels, fhi);
-    pack_fields<FMT, DP>(wl, g, flo);
-    pack_fields<FMT, DP>(wh, g, fhi);
+    uint32_t glo[GF<FMT>::kWords], ghi[GF<FMT>::kWords];
+    e8_group<FMT>(elo, slo, blo, levels, glo);
+    e8_group<FMT>(ehi, shi, bhi, levels, ghi);
+    place_group<FMT>(wl, g, glo);
+    place_group<FMT>(wh, g, ghi);
     if constexpr (RECON) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) { fl_all[g][i] = flo[i]; fh_all[g][i] = fhi[i]; }
+      for (int k = 0; k < GF<FMT>::kWords; ++k) { gl_all[g][k] = glo[k]; gh_all[g][k] = ghi[k]; }
     }
   }
 
@@ -463,7 +526,7 @@ __device__ __forceinline__ void compress_tile(const CompressArgs& a, const Tile&
       for (int g = 0; g < GT; ++g)
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const int mine_l = fl_all[g][i] - 8, mine_h = fh_all[g][i] - 8;
+          const int mine_l = group_code<FMT>(gl_all[g], i), mine_h = group_code<FMT>(gh_all[g], i);
           const int oth_l = __shfl_xor_sync(0xffffffffu, mine_l, 1);
           const int oth_h = __shfl_xor_sync(0xffffffffu, mine_h, 1);
           const int q = 8 * g + i;
@@ -489,55 +552,44 @@ __device__ __forceinline__ void compress_tile(const CompressArgs& a, const Tile&
 }
 
 // --------------------------------------------------------------------------
-// Persistent kernel: 1- or 2-stage TMA pipeline over the tile list.
+// Persistent kernel: 1- or 2-stage cp.async pipeline over the tile list.
 // --------------------------------------------------------------------------
 template <typename TIn, int D, int DP, int FMTK, int FMTV, bool RECON>
 __global__ void __launch_bounds__(kCompressThreads, 4) compress_kernel(const CompressArgs args, int n_layers,
                                                                         int n_tiles, int ns) {
   using S = Smem<TIn, D>;
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ uint64_t bar[2];
   const int first = blockIdx.x;
   if (first >= n_tiles) return;
   const int stage_bytes = S::stage(args.head_group);
   Tile cur = decode_tile(args, n_layers, first);
-  if (threadIdx.x == 0) {
-    mbar_init(&bar[0], 1);
-    mbar_init(&bar[1], 1);
-    fence_mbar_init();
-    mbar_arrive_expect_tx(&bar[0], tile_bytes<TIn, D>(args, cur));
-  }
-  __syncthreads();
-  issue_tile<TIn, D>(args, cur, smem, &bar[0]);
+  issue_tile<TIn, D>(args, cur, smem);
+  cp_async_commit();
   int it = 0;
-  // ns = 2: tile i+1 is loaded into the other stage while tile i is computed;
-  // ns = 1 (rows too large for two stages): load and compute alternate.
+  // ns = 2: tile i+1 is copied into the other stage while tile i is computed;
+  // ns = 1 (rows too large for two stages): copy and compute alternate.
   for (int tile = first; tile < n_tiles; tile += gridDim.x, ++it) {
     const int s = ns == 2 ? (it & 1) : 0;
-    const uint32_t ph = ns == 2 ? ((it >> 1) & 1) : (it & 1);
     const int next = tile + (int)gridDim.x;
     const bool has_next = next < n_tiles;
     Tile nt = cur;
     if (has_next) nt = decode_tile(args, n_layers, next);
-    __syncthreads();  // the tile that used stage s^1 (previous iteration) is finished
-    if (ns == 2 && has_next) {
-      if (threadIdx.x == 0) mbar_arrive_expect_tx(&bar[s ^ 1], tile_bytes<TIn, D>(args, nt));
-      __syncthreads();
-      issue_tile<TIn, D>(args, nt, smem + (s ^ 1) * stage_bytes, &bar[s ^ 1]);
+    if (ns == 2) {
+      __syncwarp();  // this warp is done with stage s^1 (previous tile)
+      if (has_next) issue_tile<TIn, D>(args, nt, smem + (s ^ 1) * stage_bytes);
+      cp_async_commit();
+      cp_async_wait<1>();  // everything but the newest group: the current tile has landed
+    } else {
+      cp_async_wait<0>();
     }
-    if (!mbar_wait(&bar[s], ph)) {
-      if (args.error_flag) atomicExch(args.error_flag, 1);
-      if (ns == 2 && has_next) mbar_wait(&bar[s ^ 1], ((it + 1) >> 1) & 1);  // let in-flight copies land
-      return;
-    }
+    __syncwarp();
     const uint8_t* stage = smem + s * stage_bytes;
     if (cur.kv == 0) compress_tile<TIn, D, DP, true, FMTK, RECON>(args, cur, stage);
     else compress_tile<TIn, D, DP, false, FMTV, RECON>(args, cur, stage);
     if (ns == 1 && has_next) {
-      __syncthreads();
-      if (threadIdx.x == 0) mbar_arrive_expect_tx(&bar[0], tile_bytes<TIn, D>(args, nt));
-      __syncthreads();
-      issue_tile<TIn, D>(args, nt, smem, &bar[0]);
+      __syncwarp();
+      issue_tile<TIn, D>(args, nt, smem);
+      cp_async_commit();
     }
     cur = nt;
   }

@@ -48,10 +48,11 @@ def _run_compress(k, v, kept, lk, lv, dtype=torch.float16, base=10000.0):
                              emit_scales_f32=True)[0]
 
 
+@pytest.mark.parametrize("heads", [3, 6])  # partial head groups (2 + 1, 4 + 2)
 @pytest.mark.parametrize("d", [128, 96, 64])
 @pytest.mark.parametrize("lk,lv", [(8, 4), (4, 4), (16, 2), (2, 8)])
-def test_compress_bit_exact_vs_oracle(orc, d, lk, lv):
-    cfg = syn.CacheConfig("t", 1, 2, 3, 77, d)
+def test_compress_bit_exact_vs_oracle(orc, d, lk, lv, heads):
+    cfg = syn.CacheConfig("t", 1, 2, heads, 77, d)
     k, v = syn.cpu_layer(cfg, 5)
     rng = np.random.default_rng(d + lk)
     kept = np.stack([np.sort(rng.choice(77, 37, replace=False)) for _ in range(2)])
