@@ -86,6 +86,9 @@ size_t score_workspace_bytes(int batch, int n_heads, int n_q, int seq);
 // tensor-core path (nq_score_tc.cu) for fp16 / bf16 caches
 bool score_tc_supported(const ScoreArgs& a);
 cudaError_t launch_score_tc(const ScoreArgs& a, float* colsum, void* ws, cudaStream_t s);
+// tcgen05 / TMEM path (nq_score_umma.cu) for fp16 / bf16 caches
+bool score_umma_supported(const ScoreArgs& a);
+cudaError_t launch_score_umma(const ScoreArgs& a, float* colsum, void* ws, cudaStream_t s);
 cudaError_t launch_score_colsums(const ScoreArgs& a, float* colsum, void* ws, size_t ws_bytes, cudaStream_t s);
 // out[b, t] (=|+=) weight * sum_h colsum[b, h, t] in head order.
 cudaError_t launch_reduce_heads(const float* colsum, int batch, int n_heads, int seq, float weight, int accumulate,

@@ -18,16 +18,10 @@
 //    and one HADD2 / HFMA2 removes the bias.
 //  * Scale, RoPE and sharpening run in fp32 (packed f32x2 where both lanes
 //    share the operation), in the same order and rounding as the CPU oracle.
-//  * A warp owns 32 consecutive tokens of one head.  The tile's RoPE rows are
-//    copied to shared memory by cp.async while the butterfly runs, and the
-//    warp's fp16 rows are staged in shared memory and leave as contiguous
-//    512-byte stores (thread-per-row stores reach only ~80 % of the HBM
-//    bandwidth that coalesced ones do for this 1:4 read:write mix).
 #include "nq_common.cuh"
 #include "nq_internal.h"
 
 namespace nq {
-
 
 __device__ __forceinline__ __half2 h2_bits(uint32_t u) {
   __half2 h;
@@ -62,19 +56,14 @@ __device__ __forceinline__ void load_row(const uint8_t* p, uint32_t (&w)[PB / 4]
   }
 }
 
-// Packed row bytes and words of one vector.
+// Codes of coordinates {q, q + DP/2} as half2 integers, for every q < DP/2.
+// FMT: 0 = nibbles (field = c + 8), 1 = 5-bit fields (c + 8), 2 = int8 (c).
 template <int DP, int FMT>
-struct Packed {
-  static constexpr int kBytes = FMT == 0 ? DP / 2 : (FMT == 1 ? DP * 5 / 8 : DP);
-  static constexpr int kWords = kBytes / 4;
-};
-
-// Codes of coordinates {q, q + DP/2} as half2 integers, for every q < DP/2, from the
-// row's words.  FMT: 0 = nibbles (field = c + 8), 1 = 5-bit fields (c + 8), 2 = int8 (c).
-template <int DP, int FMT>
-__device__ __forceinline__ void unpack_codes(const uint32_t (&w)[Packed<DP, FMT>::kWords], __half2 (&R)[DP / 2]) {
+__device__ __forceinline__ void unpack_codes(const uint8_t* p, __half2 (&R)[DP / 2]) {
   constexpr int HR = DP / 2;
   if constexpr (FMT == 0) {
+    uint32_t w[DP / 8];
+    load_row<DP / 2>(p, w);
 #pragma unroll
     for (int q = 0; q < HR; q += 2) {
       const int m = q >> 3, byte = (q & 7) >> 1;
@@ -83,6 +72,8 @@ __device__ __forceinline__ void unpack_codes(const uint32_t (&w)[Packed<DP, FMT>
       R[q + 1] = nibble_pair<4>(u);
     }
   } else if constexpr (FMT == 1) {
+    uint32_t w[DP * 5 / 32];
+    load_row<DP * 5 / 8>(p, w);
     constexpr int OFF = 5 * HR / 32;  // word offset of coordinate q + DP/2
 #pragma unroll
     for (int q = 0; q < HR; ++q) {
@@ -99,6 +90,8 @@ __device__ __forceinline__ void unpack_codes(const uint32_t (&w)[Packed<DP, FMT>
       R[q] = __hadd2(h2_bits((u & 0x001F001Fu) | 0x64006400u), h2_const(-1032.0f));
     }
   } else {
+    uint32_t w[DP / 4];
+    load_row<DP>(p, w);
 #pragma unroll
     for (int q = 0; q < HR; ++q) {
       const int m = q >> 2, byte = q & 3;
@@ -141,213 +134,186 @@ __device__ __forceinline__ uint32_t h2u(float a, float b) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
+__device__ __forceinline__ void st_global_v8(void* p, const uint32_t (&v)[8]) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(v[0]), "r"(v[1]), "r"(v[2]),
+               "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
+}
+
+// Scale, [RoPE, sharpen] and store coordinates [0, D) as fp16.  Chunk c (outputs W*c ..
+// W*c + W-1) is paired with chunk c + D/(2W), their RoPE partners at + D/2.  W = 16 with
+// 32-byte stores (one full sector per lane) when the rows are 32-byte aligned, else 8.
+template <int D, int DP, bool KEY, bool V8>
+__device__ __forceinline__ void finish_store(const __half2 (&R)[DP / 2], float coef, const float* cosr,
+                                             const float* sinr, float sharpen, __half* out) {
+  constexpr int DH = D / 2;
+  constexpr int W = V8 ? 16 : 8;
+  static_assert(DH % W == 0, "chunk width must divide D/2");
+  const u64 coef2 = pk(coef, coef), sh2 = pk(sharpen, sharpen);
+#pragma unroll
+  for (int c = 0; c < DH / W; ++c) {
+    uint32_t o1[W / 2], o2[W / 2];
+#pragma unroll
+    for (int u = 0; u < W; u += 2) {
+      float y1[2], y2[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int i = W * c + u + e;
+        u64 z = mul2(pk(coord<DP>(R, i), coord<DP>(R, i + DH)), coef2);  // {z1, z2}
+        if constexpr (KEY) {
+          // cosr / sinr point into shared memory
+          const float cu = cosr[i], su = sinr[i];
+          float m1, m2, n1, n2;
+          upk(mul2(z, pk(cu, cu)), m1, m2);  // z1 c, z2 c
+          upk(mul2(z, pk(su, su)), n1, n2);  // z1 s, z2 s
+          z = pk(__fsub_rn(m1, n2), __fadd_rn(n1, m2));
+          if (sharpen != 1.0f) z = mul2(z, sh2);
+        }
+        upk(z, y1[e], y2[e]);
+      }
+      o1[u / 2] = h2u(y1[0], y1[1]);
+      o2[u / 2] = h2u(y2[0], y2[1]);
+    }
+    if constexpr (V8) {
+      st_global_v8(out + W * c, o1);
+      st_global_v8(out + DH + W * c, o2);
+    } else {
+      reinterpret_cast<uint4*>(out)[c] = make_uint4(o1[0], o1[1], o1[2], o1[3]);
+      reinterpret_cast<uint4*>(out + DH)[c] = make_uint4(o2[0], o2[1], o2[2], o2[3]);
+    }
+  }
+}
+
+// --------------------------------------------------------------------------
+// One CTA: HG heads x (128 / HG) tokens of one (layer, K|V, batch); one thread per vector.
+// --------------------------------------------------------------------------
+// RoPE rows of a tile in shared memory: per token cos[D/2] then sin[D/2], rows padded by
+// 16 bytes so the HG-lane broadcasts of different tokens fall in different banks.
+template <int D>
+struct RopeSmem {
+  static constexpr int kRow = 4 * D + 16;
+  static constexpr int kChunks = 4 * D / 16;  // 16-byte chunks per token (cos + sin)
+};
+
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
 }
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
 }
-__device__ __forceinline__ void st_shared_v4(void* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(p)), "r"(a), "r"(b), "r"(c), "r"(d)
-               : "memory");
-}
-__device__ __forceinline__ float4 ld_shared_f4(const void* p) {
-  float4 v;
-  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(smem_u32(p)));
-  return v;
-}
-__device__ __forceinline__ uint4 ld_shared_u4(const void* p) {
-  uint4 v;
-  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "r"(smem_u32(p)));
-  return v;
-}
 
-// --------------------------------------------------------------------------
-// Tile geometry.  A CTA of 4 warps covers HGT heads x (128 / HGT) tokens of one
-// (layer, K|V, batch), HGT = min(4, head_group); warp w takes head w % HGT and the
-// 32 consecutive tokens of block w / HGT, one token per lane.  A warp's output rows
-// are then one head's consecutive tokens: they go through shared memory and leave
-// as 512-byte contiguous stores, and its code rows / scales are contiguous loads.
-// --------------------------------------------------------------------------
-template <int D>
-struct DqSmem {
-  static constexpr int kOutRow = 2 * D + 16;                 // fp16 row + pad (conflict-free 16-byte access)
-  static constexpr int kOut = 4 * 32 * kOutRow;              // staging of the 4 warps
-  static constexpr int kRopeRow = 4 * D + 16;                // cos[D/2], sin[D/2], pad
-  static constexpr int kRopeChunks = 4 * D / 16;
-  static int bytes(int hgt) { return kOut + (128 / hgt) * kRopeRow; }
-};
-
-__host__ __device__ __forceinline__ int dq_heads_per_tile(int head_group) { return head_group < 4 ? head_group : 4; }
-static inline int dq_heads_per_tile_host(int head_group) { return dq_heads_per_tile(head_group); }
-
-// Scale, [RoPE, sharpen], convert to fp16 and write the row into shared memory.  Output
-// chunk c (outputs 8c .. 8c+7) is paired with chunk c + D/16 (RoPE partners at + D/2).
-template <int D, int DP, bool KEY, bool SHARP>
-__device__ __forceinline__ void finish_row(const __half2 (&R)[DP / 2], float coef, const uint8_t* trow,
-                                           float sharpen, uint8_t* srow) {
-  constexpr int DH = D / 2;
-  const u64 coef2 = pk(coef, coef), sh2 = pk(sharpen, sharpen);
-#pragma unroll
-  for (int c = 0; c < DH / 8; ++c) {
-    uint32_t o1[4], o2[4];
-#pragma unroll
-    for (int u = 0; u < 8; u += 4) {
-      float4 cv = make_float4(0.f, 0.f, 0.f, 0.f), sv = cv;
-      if constexpr (KEY) {
-        cv = ld_shared_f4(trow + 4 * (8 * c + u));
-        sv = ld_shared_f4(trow + 4 * (DH + 8 * c + u));
-      }
-      const float cc[4] = {cv.x, cv.y, cv.z, cv.w}, ss[4] = {sv.x, sv.y, sv.z, sv.w};
-      float y1[4], y2[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int i = 8 * c + u + e;
-        u64 z = mul2(pk(coord<DP>(R, i), coord<DP>(R, i + DH)), coef2);  // {z1, z2}
-        if constexpr (KEY) {
-          float m1, m2, n1, n2;
-          upk(mul2(z, pk(cc[e], cc[e])), m1, m2);  // z1 c, z2 c
-          upk(mul2(z, pk(ss[e], ss[e])), n1, n2);  // z1 s, z2 s
-          z = pk(__fsub_rn(m1, n2), __fadd_rn(n1, m2));
-          if constexpr (SHARP) z = mul2(z, sh2);
-        }
-        upk(z, y1[e], y2[e]);
-      }
-      o1[u / 2] = h2u(y1[0], y1[1]); o1[u / 2 + 1] = h2u(y1[2], y1[3]);
-      o2[u / 2] = h2u(y2[0], y2[1]); o2[u / 2 + 1] = h2u(y2[2], y2[3]);
-    }
-    st_shared_v4(srow + 16 * c, o1[0], o1[1], o1[2], o1[3]);
-    st_shared_v4(srow + 2 * DH + 16 * c, o2[0], o2[1], o2[2], o2[3]);
-  }
-}
-
-template <int D, int DP, bool KEY, int FMT, bool SHARP>
-__device__ __forceinline__ void decompress_tile(const DecompressArgs& args, const DLayerIO& L, int b, int hgi,
-                                                int tt, int count, uint8_t* smem) {
-  using S = DqSmem<D>;
-  constexpr int DH = D / 2;
-  const int HGT = dq_heads_per_tile(args.head_group);
-  const int TOK = kCompressThreads / HGT;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int head = hgi * HGT + warp % HGT;
-  const int j0w = tt * TOK + (warp / HGT) * 32;  // first token of this warp
-  const int j = j0w + lane;
-  const bool valid = j < count && head < args.heads;
-  uint8_t* rope = smem + S::kOut;
+template <int D, int DP, bool KEY, int FMT, bool V8>
+__device__ __forceinline__ void decompress_vector(const DecompressArgs& args, const DLayerIO& L, int b, int head,
+                                                  int j, bool valid, uint8_t* rope_smem) {
   const int64_t vrow = ((int64_t)b * args.heads + head) * args.n_tokens + j;
-  using P = Packed<DP, FMT>;
-  uint32_t w[P::kWords];
-  uint16_t sbits = 0;
-  if (valid) {
-    load_row<P::kBytes>((KEY ? L.k_codes : L.v_codes) + vrow * P::kBytes, w);
-    sbits = (KEY ? L.k_scales : L.v_scales)[vrow];
-  }
+  constexpr int DH = D / 2;
+  const int HG = args.head_group;
+  float* trow = nullptr;
   if constexpr (KEY) {
-    // cos / sin rows of the tile's tokens -> shared memory, overlapping the code loads and
-    // the butterfly: the CTA's threads split evenly over the tile's tokens, one position each
-    const int tok0 = tt * TOK;
-    const int n_tok = min(TOK, count - tok0);
-    const int tpt = kCompressThreads / TOK;  // threads per token (1, 2 or 4)
-    const int t = threadIdx.x / tpt;
-    if (t < n_tok) {
-      const int pos = args.positions[(int64_t)b * args.n_tokens + tok0 + t];
-      for (int k = threadIdx.x % tpt; k < S::kRopeChunks; k += tpt) {
-        const int half = k / (S::kRopeChunks / 2), q = k % (S::kRopeChunks / 2);
-        cp_async16(rope + t * S::kRopeRow + half * 4 * DH + 16 * q,
-                   (half ? args.rope_sin : args.rope_cos) + (int64_t)pos * DH + 4 * q);
+    // the HG threads of this token copy its cos / sin rows into shared memory while the
+    // butterfly runs (they are consecutive lanes of one warp)
+    trow = reinterpret_cast<float*>(rope_smem + (threadIdx.x / HG) * RopeSmem<D>::kRow);
+    if (valid) {
+      const int pos = args.positions[(int64_t)b * args.n_tokens + j];
+      const int hl = threadIdx.x % HG;
+      for (int c = hl; c < RopeSmem<D>::kChunks; c += HG) {
+        const int half = c / (RopeSmem<D>::kChunks / 2), k = c % (RopeSmem<D>::kChunks / 2);
+        const float* src = (half ? args.rope_sin : args.rope_cos) + (int64_t)pos * DH + 4 * k;
+        cp_async16(trow + half * DH + 4 * k, src);
       }
     }
   }
+  constexpr int PB = FMT == 0 ? DP / 2 : (FMT == 1 ? DP * 5 / 8 : DP);
   __half2 R[DP / 2];
   float coef = 0.0f;
   if (valid) {
-    unpack_codes<DP, FMT>(w, R);
+    unpack_codes<DP, FMT>((KEY ? L.k_codes : L.v_codes) + vrow * PB, R);
     fwht_half2<DP>(R);
-    coef = __fmul_rn(__half2float(__ushort_as_half(sbits)), 0.5f * hadamard_entry(DP));
+    const float scale = __half2float(__ushort_as_half((KEY ? L.k_scales : L.v_scales)[vrow]));
+    coef = __fmul_rn(scale, 0.5f * hadamard_entry(DP));
   }
   if constexpr (KEY) {
     cp_async_wait_all();
-    __syncthreads();  // rope rows are shared across warps
+    __syncwarp();
   }
-  uint8_t* sw = smem + warp * 32 * S::kOutRow;
-  if (valid)
-    finish_row<D, DP, KEY, SHARP>(R, coef, rope + ((warp / HGT) * 32 + lane) * S::kRopeRow, args.key_sharpen,
-                                  sw + lane * S::kOutRow);
-  __syncwarp();
-  // the warp's rows leave as 16-byte chunks, each row written by 2*D/16 consecutive lanes
-  if (head < args.heads) {
-    constexpr int CPR = 2 * D / 16;  // chunks per row
-    constexpr int RPI = 32 / CPR;    // rows per instruction
-    __half* base = reinterpret_cast<__half*>(KEY ? L.k_out : L.v_out) + (int64_t)b * args.out_stride_b +
-                   (int64_t)head * args.out_stride_h;
-    const int cr = lane % CPR;
-#pragma unroll
-    for (int k = 0; k < 32 / RPI; ++k) {
-      const int r = k * RPI + lane / CPR;
-      if (j0w + r < count) {
-        const uint4 v = ld_shared_u4(sw + r * S::kOutRow + 16 * cr);
-        reinterpret_cast<uint4*>(base + (int64_t)(j0w + r) * args.out_stride_t)[cr] = v;
-      }
-    }
-  }
+  if (!valid) return;
+  __half* o = reinterpret_cast<__half*>(KEY ? L.k_out : L.v_out) + (int64_t)b * args.out_stride_b +
+              (int64_t)head * args.out_stride_h + (int64_t)j * args.out_stride_t;
+  finish_store<D, DP, KEY, V8>(R, coef, trow, trow + DH, args.key_sharpen, o);
 }
 
-template <int D, int DP, bool SHARP>
+template <int D, int DP, bool V8>
 __global__ void __launch_bounds__(kCompressThreads, 4) decompress_kernel(const DecompressArgs args) {
-  extern __shared__ __align__(16) uint8_t smem[];
-  const int HGT = dq_heads_per_tile(args.head_group);
-  const int TOK = kCompressThreads / HGT;
+  extern __shared__ __align__(16) uint8_t rope_smem[];
+  const int HG = args.head_group;
+  const int TOK = kCompressThreads / HG;
   int bid = blockIdx.x;
   const int t_tiles = (args.n_tokens + TOK - 1) / TOK;
-  const int h_groups = (args.heads + HGT - 1) / HGT;
+  const int h_groups = (args.heads + HG - 1) / HG;
   const int tt = bid % t_tiles; bid /= t_tiles;
-  const int hgi = bid % h_groups; bid /= h_groups;
+  const int hg = bid % h_groups; bid /= h_groups;
   const int b = bid % args.batch; bid /= args.batch;
   const int kv = bid & 1;
   const int layer = bid >> 1;
   const DLayerIO& L = args.layers[layer];
   const bool key = kv == 0;
   if ((key ? L.k_codes : L.v_codes) == nullptr) return;
+  const int j = tt * TOK + threadIdx.x / HG;
+  const int head = hg * HG + threadIdx.x % HG;
   const int count = args.count ? min(args.count[b], args.n_tokens) : args.n_tokens;
-  if (tt * TOK >= count) return;  // uniform over the CTA
+  // invalid threads stay until the warp-level barrier of the key path
+  const bool valid = j < count && head < args.heads;
   const int levels = key ? L.key_levels : L.value_levels;
   const int fmt = levels <= 4 ? 0 : (levels == 8 ? 1 : 2);
   if (key) {
-    if (fmt == 0) decompress_tile<D, DP, true, 0, SHARP>(args, L, b, hgi, tt, count, smem);
-    else if (fmt == 1) decompress_tile<D, DP, true, 1, SHARP>(args, L, b, hgi, tt, count, smem);
-    else decompress_tile<D, DP, true, 2, SHARP>(args, L, b, hgi, tt, count, smem);
+    if (fmt == 0) decompress_vector<D, DP, true, 0, V8>(args, L, b, head, j, valid, rope_smem);
+    else if (fmt == 1) decompress_vector<D, DP, true, 1, V8>(args, L, b, head, j, valid, rope_smem);
+    else decompress_vector<D, DP, true, 2, V8>(args, L, b, head, j, valid, rope_smem);
   } else {
-    if (fmt == 0) decompress_tile<D, DP, false, 0, SHARP>(args, L, b, hgi, tt, count, smem);
-    else if (fmt == 1) decompress_tile<D, DP, false, 1, SHARP>(args, L, b, hgi, tt, count, smem);
-    else decompress_tile<D, DP, false, 2, SHARP>(args, L, b, hgi, tt, count, smem);
+    if (fmt == 0) decompress_vector<D, DP, false, 0, V8>(args, L, b, head, j, valid, rope_smem);
+    else if (fmt == 1) decompress_vector<D, DP, false, 1, V8>(args, L, b, head, j, valid, rope_smem);
+    else decompress_vector<D, DP, false, 2, V8>(args, L, b, head, j, valid, rope_smem);
   }
 }
 
-template <int D, int DP>
-static cudaError_t launch_dq(const DecompressArgs& a, long long blocks, cudaStream_t s) {
-  const int smem = DqSmem<D>::bytes(dq_heads_per_tile_host(a.head_group));
-  auto kern = a.key_sharpen != 1.0f ? decompress_kernel<D, DP, true> : decompress_kernel<D, DP, false>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+template <int D, int DP, bool V8>
+static cudaError_t launch_dq_t(const DecompressArgs& a, long long blocks, cudaStream_t s) {
+  const int smem = (kCompressThreads / a.head_group) * RopeSmem<D>::kRow;
+  cudaError_t e =
+      cudaFuncSetAttribute(decompress_kernel<D, DP, V8>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  kern<<<(unsigned)blocks, kCompressThreads, smem, s>>>(a);
+  decompress_kernel<D, DP, V8><<<(int)blocks, kCompressThreads, smem, s>>>(a);
   return cudaGetLastError();
+}
+
+// 32-byte stores need every output row and half-row to start on a 32-byte boundary.
+static bool rows_32b_aligned(const DecompressArgs& a, int n_layers) {
+  if ((a.out_stride_b * 2) % 32 || (a.out_stride_h * 2) % 32 || (a.out_stride_t * 2) % 32 || a.head_dim % 32)
+    return false;
+  for (int l = 0; l < n_layers; ++l) {
+    if ((reinterpret_cast<uintptr_t>(a.layers[l].k_out) | reinterpret_cast<uintptr_t>(a.layers[l].v_out)) & 31)
+      return false;
+  }
+  return true;
+}
+
+template <int D, int DP>
+static cudaError_t launch_dq(const DecompressArgs& a, int n_layers, long long blocks, cudaStream_t s) {
+  return rows_32b_aligned(a, n_layers) ? launch_dq_t<D, DP, true>(a, blocks, s) : launch_dq_t<D, DP, false>(a, blocks, s);
 }
 
 // --------------------------------------------------------------------------
 // Launcher
 // --------------------------------------------------------------------------
 cudaError_t launch_decompress(const DecompressArgs& a, int n_layers, cudaStream_t s) {
-  const int hgt = dq_heads_per_tile_host(a.head_group);
-  const int tok = kCompressThreads / hgt;
-  const long long blocks = (long long)n_layers * 2 * a.batch * ((a.heads + hgt - 1) / hgt) *
+  const int tok = kCompressThreads / a.head_group;
+  const long long blocks = (long long)n_layers * 2 * a.batch * ((a.heads + a.head_group - 1) / a.head_group) *
                            ((a.n_tokens + tok - 1) / tok);
   if (blocks <= 0) return cudaSuccess;
   if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
-  if (a.head_dim == 128 && a.head_dim_padded == 128) return launch_dq<128, 128>(a, blocks, s);
-  if (a.head_dim == 96 && a.head_dim_padded == 128) return launch_dq<96, 128>(a, blocks, s);
-  if (a.head_dim == 64 && a.head_dim_padded == 64) return launch_dq<64, 64>(a, blocks, s);
+  if (a.head_dim == 128 && a.head_dim_padded == 128) return launch_dq<128, 128>(a, n_layers, blocks, s);
+  if (a.head_dim == 96 && a.head_dim_padded == 128) return launch_dq<96, 128>(a, n_layers, blocks, s);
+  if (a.head_dim == 64 && a.head_dim_padded == 64) return launch_dq<64, 64>(a, n_layers, blocks, s);
   return cudaErrorInvalidValue;
 }
 
