@@ -83,9 +83,6 @@ struct ScoreArgs {
 };
 size_t score_workspace_bytes(int batch, int n_heads, int n_q, int seq);
 // Per-head column sums colsum[b, h - head_begin, t] into the workspace-backed buffer `colsum`.
-// tensor-core path (nq_score_tc.cu) for fp16 / bf16 caches
-bool score_tc_supported(const ScoreArgs& a);
-cudaError_t launch_score_tc(const ScoreArgs& a, float* colsum, void* ws, cudaStream_t s);
 // tcgen05 / TMEM path (nq_score_umma.cu) for fp16 / bf16 caches
 bool score_umma_supported(const ScoreArgs& a);
 cudaError_t launch_score_umma(const ScoreArgs& a, float* colsum, void* ws, cudaStream_t s);
