@@ -35,7 +35,7 @@
 extern "C" {
 #endif
 
-#define NQ_ABI_VERSION 1
+#define NQ_ABI_VERSION 2
 
 typedef int32_t nq_status_t;
 enum {
@@ -110,7 +110,12 @@ typedef struct nq_compress_params {
   int32_t rotate;                /* 1: Walsh-Hadamard rotation (the pipelines' path);
                                     0: quantize the (RoPE-removed) rows as given, as
                                        E8Lattice.quantize_perhead does (e8_lattice.py:97-124) */
-  int32_t *error_flag;           /* optional device int32, set to 1 when a bounded wait expires */
+  int32_t inputs_host;           /* 0: k / v are device memory.  1: k / v are pinned host memory
+                                    mapped into the device address space (UVA: the host pointer
+                                    is the device pointer); the kernel then reads only the kept
+                                    rows across PCIe.  Checked with cudaPointerGetAttributes:
+                                    anything else returns NQ_ERR_INVALID_ARG. */
+  int32_t *error_flag;           /* optional device int32 (reserved; no bounded wait sets it) */
   const nq_layer_io_t *layers;   /* HOST array [n_layers] */
   int32_t n_layers;
 } nq_compress_params_t;

@@ -49,7 +49,7 @@ class CompressParams(ctypes.Structure):
                 ("in_dtype", c_i32), ("in_stride_b", c_i64), ("in_stride_h", c_i64), ("in_stride_t", c_i64),
                 ("out_stride_b", c_i64), ("out_stride_h", c_i64), ("out_stride_t", c_i64),
                 ("out_row_mode", c_i32), ("out_positions", c_vp), ("key_sharpen", c_f32),
-                ("rotate", c_i32), ("error_flag", c_vp), ("layers", ctypes.POINTER(LayerIO)), ("n_layers", c_i32)]
+                ("rotate", c_i32), ("inputs_host", c_i32), ("error_flag", c_vp), ("layers", ctypes.POINTER(LayerIO)), ("n_layers", c_i32)]
 
 
 class DLayerIO(ctypes.Structure):
@@ -114,7 +114,7 @@ def load(path: str = LIB_PATH):
                 fn = getattr(lib, name)
                 fn.restype = res
                 fn.argtypes = args
-            if lib.nq_abi_version() != 1:
+            if lib.nq_abi_version() != 2:
                 raise ImportError("nexusquant_b200 native library ABI mismatch")
             _lib = lib
     return _lib

@@ -71,6 +71,18 @@ nq_status_t nq_compress_layers(const nq_compress_params_t* p, nq_stream_t stream
     for (const void* q : ptrs)
       if (q && !aligned16(q)) return NQ_ERR_ALIGNMENT;
     if ((L.k_codes && !L.k) || (L.v_codes && !L.v)) return NQ_ERR_INVALID_ARG;
+    if (p->inputs_host) {
+      // host-resident layers must be pinned and mapped at the same address (UVA)
+      for (const void* q : {L.k, L.v}) {
+        if (!q) continue;
+        cudaPointerAttributes at;
+        if (cudaPointerGetAttributes(&at, q) != cudaSuccess || at.type != cudaMemoryTypeHost ||
+            at.devicePointer != q) {
+          cudaGetLastError();
+          return NQ_ERR_INVALID_ARG;
+        }
+      }
+    }
     any_key |= (L.k != nullptr);
     any_out |= (L.k_out || L.v_out);
   }

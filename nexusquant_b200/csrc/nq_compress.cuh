@@ -296,41 +296,59 @@ template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 // Copy one tile's rows (and, for keys, its tokens' RoPE rows) into a stage with 16-byte
-// cp.async: the two threads of vector v copy alternate chunks of row v, and the 2*HG
-// threads of a token share its cos / sin rows.  Every region of the stage is written and
-// read by lanes of one warp, so a warp barrier orders the copies and their readers.
+// cp.async.  A warp copies exactly the rows of its own 16 vectors (and of their tokens), so
+// a warp barrier orders the copies and their readers; consecutive lanes take consecutive
+// chunks of a row, so every copy instruction moves whole contiguous rows (good coalescing,
+// and few large reads when the layers sit in host memory behind PCIe).
 template <typename TIn, int D>
 __device__ __forceinline__ void issue_tile(const CompressArgs& a, const Tile& t, uint8_t* stage) {
   using S = Smem<TIn, D>;
+  constexpr int CPR = S::kRowBytes / 16;  // 16-byte chunks per row
+  constexpr int WV = 16;                  // vectors per warp
   const LayerIO& L = a.layers[t.layer];
   const bool key = t.kv == 0;
   const TIn* src = static_cast<const TIn*>(key ? L.k : L.v);
+  if (src == nullptr) return;
   const int HG = a.head_group, TOK = kCompressVecs / HG;
   const int count = a.kept_count ? min(a.kept_count[t.b], a.n_kept) : a.n_kept;
-  const int v = threadIdx.x >> 1, h = threadIdx.x & 1;
+  const int lane = threadIdx.x & 31, wv0 = (threadIdx.x >> 5) * WV;  // the warp's first vector
+  // this lane's vector (lanes 2v, 2v+1 own vector v): its row address and RoPE position
+  const int v = threadIdx.x >> 1;
   const int tok_l = v / HG, head_l = v % HG;
   const int j = t.tt * TOK + tok_l;
   const int head = t.hg * HG + head_l;
-  if (src == nullptr || j >= count) return;
-  const int row = a.kept_idx ? a.kept_idx[(int64_t)t.b * a.n_kept + j] : j;
+  const bool vj = j < count;
+  const int row = vj ? (a.kept_idx ? a.kept_idx[(int64_t)t.b * a.n_kept + j] : j) : 0;
+  const bool valid = vj && head < a.heads;
+  const uint8_t* g = valid ? reinterpret_cast<const uint8_t*>(src + (int64_t)t.b * a.in_stride_b +
+                                                              (int64_t)head * a.in_stride_h +
+                                                              (int64_t)row * a.in_stride_t)
+                           : nullptr;
+#pragma unroll
+  for (int i = 0; i < WV * CPR / 32; ++i) {
+    const int c = i * 32 + lane;
+    const int rv = c / CPR, ck = c % CPR;  // row (vector) within the warp, chunk within the row
+    const uint8_t* gr = reinterpret_cast<const uint8_t*>(
+        __shfl_sync(0xffffffffu, reinterpret_cast<uintptr_t>(g), 2 * rv));
+    if (gr) cp_async16(stage + (wv0 + rv) * S::kRowStride + 16 * ck, gr + 16 * ck);
+  }
   if (key) {
-    // every lane of the token's group copies, whether or not its own head exists
+    // the warp's tokens: vectors wv0 .. wv0+15 -> tokens wv0/HG .. (wv0+15)/HG
     constexpr int HALF = (D / 2) * 4 / 16;  // chunks of one cos (or sin) row
-    const int pos = a.positions ? a.positions[(int64_t)t.b * a.n_kept + j] : row;
-    uint8_t* trow = stage + S::kRows + tok_l * S::kTabStride;
-    const float* cs = a.rope_cos + (int64_t)pos * (D / 2);
-    const float* sn = a.rope_sin + (int64_t)pos * (D / 2);
-    for (int c = 2 * head_l + h; c < 2 * HALF; c += 2 * HG) {
-      if (c < HALF) cp_async16(trow + 16 * c, cs + 4 * c);
-      else cp_async16(trow + 16 * c, sn + 4 * (c - HALF));
+    const int pos = vj ? (a.positions ? a.positions[(int64_t)t.b * a.n_kept + j] : row) : -1;
+    const int tw0 = wv0 / HG, ntw = (WV + HG - 1) / HG;  // tokens of this warp
+    const int n_chunks = ntw * 2 * HALF;
+    for (int c0 = 0; c0 < n_chunks; c0 += 32) {  // uniform trip count: the shuffle needs every lane
+      const int c = c0 + lane;
+      const int tk = min(c / (2 * HALF), ntw - 1), k = c % (2 * HALF);
+      // position of token tw0 + tk, held by the lanes of its first vector (HG divides 16)
+      const int p = __shfl_sync(0xffffffffu, pos, 2 * tk * HG);
+      if (c >= n_chunks || p < 0 || tw0 + tk >= TOK) continue;
+      uint8_t* trow = stage + S::kRows + (tw0 + tk) * S::kTabStride;
+      if (k < HALF) cp_async16(trow + 16 * k, a.rope_cos + (int64_t)p * (D / 2) + 4 * k);
+      else cp_async16(trow + 16 * k, a.rope_sin + (int64_t)p * (D / 2) + 4 * (k - HALF));
     }
   }
-  if (head >= a.heads) return;
-  const uint8_t* g = reinterpret_cast<const uint8_t*>(src + (int64_t)t.b * a.in_stride_b +
-                                                      (int64_t)head * a.in_stride_h + (int64_t)row * a.in_stride_t);
-  uint8_t* dst = stage + v * S::kRowStride;
-#pragma unroll
-  for (int c = h; c < S::kRowBytes / 16; c += 2) cp_async16(dst + 16 * c, g + 16 * c);
 }
 
 // --------------------------------------------------------------------------

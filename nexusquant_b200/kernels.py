@@ -85,7 +85,8 @@ def compress_layers(ks: Sequence[Optional[torch.Tensor]], vs: Sequence[Optional[
                     recon_v: Optional[Sequence[Optional[torch.Tensor]]] = None,
                     recon_rows: str = "source", recon_positions: Optional[torch.Tensor] = None,
                     key_sharpen: float = 1.0, rope_rows: Optional[int] = None,
-                    codes_out: Optional[Sequence[LayerCodes]] = None, rotate: bool = True) -> List[LayerCodes]:
+                    codes_out: Optional[Sequence[LayerCodes]] = None, rotate: bool = True,
+                    device: Optional[torch.device] = None) -> List[LayerCodes]:
     """Compress several layers that share one keep set in a single kernel launch.
 
     ks / vs   : per-layer [b, h, T, d] tensors (same shape, dtype, strides); None skips that half.
@@ -101,8 +102,18 @@ def compress_layers(ks: Sequence[Optional[torch.Tensor]], vs: Sequence[Optional[
     ref = next((t for t in list(ks) + list(vs) if t is not None), None)
     if ref is None:
         return []
-    _require_cuda(ref, kept_idx, kept_count, positions)
-    dev = ref.device
+    host_in = not ref.is_cuda
+    if host_in:
+        # layers in pinned host memory: the kernel reads only the kept rows, over PCIe
+        if not all(t.is_pinned() for t in list(ks) + list(vs) if t is not None):
+            raise RuntimeError("host-resident layers must be in pinned memory")
+        if device is None:
+            raise ValueError("device= is required when the layers are in host memory")
+        dev = torch.device(device)
+    else:
+        _require_cuda(ref)
+        dev = ref.device
+    _require_cuda(kept_idx, kept_count, positions)
     b, h, T, d = ref.shape
     if ref.dtype not in _DTYPES:
         raise TypeError(f"unsupported cache dtype {ref.dtype}")
@@ -184,6 +195,7 @@ def compress_layers(ks: Sequence[Optional[torch.Tensor]], vs: Sequence[Optional[
     p.out_positions = _ptr(recon_positions)
     p.key_sharpen = float(key_sharpen)
     p.rotate = int(bool(rotate))
+    p.inputs_host = int(host_in)
     p.error_flag = None
     p.layers = ctypes.cast(arr, ctypes.POINTER(N.LayerIO))
     p.n_layers = L

@@ -29,7 +29,7 @@ def test_library_exports_header_symbols():
 
 def test_abi_version_and_status_strings():
     lib = N.load()
-    assert lib.nq_abi_version() == 1
+    assert lib.nq_abi_version() == 2
     assert lib.nq_status_string(0) == b"ok"
     assert lib.nq_status_string(-6).startswith(b"pointer")
     assert lib.nq_packed_bytes(128, 8) == 80
