@@ -279,6 +279,16 @@ nq_status_t nq_gather_rows(const void* in, int32_t in_dtype, int32_t batch, int3
   if (!aligned16(in) || !aligned16(out) || (in_stride_b * eb) % 16 || (in_stride_h * eb) % 16 ||
       (in_stride_t * eb) % 16 || (out_stride_b * 2) % 16 || (out_stride_h * 2) % 16 || (out_stride_t * 2) % 16)
     return NQ_ERR_ALIGNMENT;
+  {
+    // device memory, or pinned host memory mapped at the same address (UVA); nothing else
+    cudaPointerAttributes at;
+    if (cudaPointerGetAttributes(&at, in) != cudaSuccess ||
+        (at.type != cudaMemoryTypeDevice && at.type != cudaMemoryTypeManaged &&
+         !(at.type == cudaMemoryTypeHost && at.devicePointer == in))) {
+      cudaGetLastError();
+      return NQ_ERR_INVALID_ARG;
+    }
+  }
   return cuda_status(nq::launch_gather_rows(in, in_dtype, batch, heads, head_dim, in_stride_b, in_stride_h,
                                             in_stride_t, kept_idx, kept_count, n_kept, out, out_stride_b,
                                             out_stride_h, out_stride_t, static_cast<cudaStream_t>(stream)));

@@ -333,18 +333,26 @@ def select_keep(importance: torch.Tensor, sliding_window: int, n_keep: int,
 
 
 def gather_rows(x: torch.Tensor, kept_idx: Optional[torch.Tensor], n_kept: int,
-                kept_count: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """fp16 copy of the kept rows: out[b, h, j] = x[b, h, kept_idx[b, j]]."""
-    _require_cuda(x, kept_idx, kept_count)
-    x = _rowmajor(x)
+                kept_count: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+                device: Optional[torch.device] = None) -> torch.Tensor:
+    """fp16 copy of the kept rows: out[b, h, j] = x[b, h, kept_idx[b, j]].  x may be in pinned
+    host memory (pass device=): only the kept rows then cross PCIe."""
+    _require_cuda(kept_idx, kept_count)
+    if x.is_cuda:
+        dev = x.device
+        x = _rowmajor(x)
+    else:
+        if not x.is_pinned() or device is None:
+            raise RuntimeError("host-resident input must be pinned, with device= given")
+        dev = torch.device(device)
     b, h, T, d = x.shape
     if out is None:
-        out = torch.empty((b, h, n_kept, d), dtype=torch.float16, device=x.device)
+        out = torch.empty((b, h, n_kept, d), dtype=torch.float16, device=dev)
     if kept_idx is not None:
         kept_idx = kept_idx.to(dtype=torch.int32).contiguous()
     s, o = x.stride(), out.stride()
     N.call("nq_gather_rows", x.data_ptr(), _DTYPES[x.dtype], b, h, d, s[0], s[1], s[2], _ptr(kept_idx),
-           _ptr(kept_count), n_kept, out.data_ptr(), o[0], o[1], o[2], _stream(x.device))
+           _ptr(kept_count), n_kept, out.data_ptr(), o[0], o[1], o[2], _stream(dev))
     return out
 
 

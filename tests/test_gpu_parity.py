@@ -292,3 +292,28 @@ def test_gather_and_delta(orc):
         d = K.delta_codes(packed, 128, lv).cpu().numpy()
         codes = orc.unpack(packed.cpu().numpy().reshape(-1, packed.shape[-1]), 128, lv).reshape(2, 5, 128)
         assert np.array_equal(d.reshape(2, 5, 128), orc.delta(codes))
+
+
+def test_host_resident_inputs_match_device(orc):
+    """Layers in pinned host memory: compress and gather read only the kept rows across PCIe
+    and give the same bytes as device-resident layers; pageable memory is refused."""
+    cfg = syn.CacheConfig("t", 1, 2, 4, 300, 128)
+    k, v = syn.cpu_layer(cfg, 4)
+    kd, vd = k.to(DEV), v.to(DEV)
+    hk, hv = k.pin_memory(), v.pin_memory()
+    rng = np.random.default_rng(3)
+    kept = torch.as_tensor(np.stack([np.sort(rng.choice(300, 111, replace=False)) for _ in range(2)]),
+                           dtype=torch.int32, device=DEV)
+    ref = K.compress_layers([kd], [vd], key_levels=8, value_levels=4, kept_idx=kept)[0]
+    got = K.compress_layers([hk], [hv], key_levels=8, value_levels=4, kept_idx=kept, device=DEV)[0]
+    for a, b in ((ref.k_codes, got.k_codes), (ref.v_codes, got.v_codes), (ref.k_scales, got.k_scales),
+                 (ref.v_scales, got.v_scales)):
+        assert torch.equal(a, b)
+    assert torch.equal(K.gather_rows(kd, kept, 111), K.gather_rows(hk, kept, 111, device=DEV))
+    with pytest.raises(RuntimeError):
+        K.compress_layers([k], [v], key_levels=8, value_levels=4, kept_idx=kept, device=DEV)  # not pinned
+    from nexusquant_b200 import _native as N
+    with pytest.raises(RuntimeError):  # the C ABI itself refuses pageable host memory
+        N.call("nq_gather_rows", k.data_ptr(), 0, 2, 4, 128, *k.stride()[:3], kept.data_ptr(), None, 111,
+               torch.empty((2, 4, 111, 128), dtype=torch.float16, device=DEV).data_ptr(), 4 * 111 * 128,
+               111 * 128, 128, None)
