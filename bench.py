@@ -394,6 +394,12 @@ def main():
     ap.add_argument("--profile", action="store_true", help="a few steps only (for ncu launch lists)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    # Native libraries (NCCL's version banner, for one) print to fd 1; the driver reads the one
+    # JSON line from stdout, so fd 1 is pointed at stderr and the line goes to the saved stdout.
+    sys.stdout.flush()
+    out = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
+    sys.stdout = out
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
