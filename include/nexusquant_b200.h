@@ -256,6 +256,36 @@ nq_status_t nq_gather_rows(const void *in, int32_t in_dtype, int32_t batch, int3
 nq_status_t nq_delta_codes(const uint8_t *codes, int32_t n_streams, int32_t n_tokens, int32_t head_dim_padded,
                            int32_t levels, int8_t *delta, nq_stream_t stream);
 
+/*
+ * Decode attention straight from the compressed layout: one query token per sequence,
+ * softmax(q K^T * scale) V with K / V dequantized on the fly as nq_decompress_layers
+ * would (keys re-rotated at their positions, sharpened, rounded to fp16), fp16 output.
+ * Replaces NexusQuantPagedAttention.forward (vllm_backend.py:692-765), which
+ * decompresses every page to fp16 first.  head_dim = head_dim_padded = 128; query head
+ * g*G + i attends KV head g, G = q_heads / heads in {1, 2, 4, 8}; a sequence with
+ * count 0 gets a zero output, as in the reference.
+ */
+typedef struct {
+  int32_t batch, q_heads, heads, head_dim, head_dim_padded, n_tokens;
+  const int32_t *count;          /* [batch] valid tokens (<= n_tokens); NULL = n_tokens */
+  const uint16_t *q;             /* fp16 [batch, q_heads, head_dim], row stride 1 */
+  int64_t q_stride_b, q_stride_h;
+  const uint8_t *k_codes, *v_codes;      /* [batch, heads, n_tokens, packed bytes] */
+  const uint16_t *k_scales, *v_scales;   /* fp16 [batch, heads, n_tokens] */
+  int32_t key_levels, value_levels;
+  const int32_t *positions;      /* [batch, n_tokens] RoPE positions of the stored keys */
+  const float *rope_cos, *rope_sin;  /* [rope_rows, head_dim/2], as for nq_compress_layers */
+  int32_t rope_rows;
+  float key_sharpen;             /* 1.0 = off */
+  float scale;                   /* logit scale; 0 = 1/sqrt(head_dim) as the reference */
+  uint16_t *out;                 /* fp16 [batch, q_heads, head_dim], row stride 1 */
+  int64_t out_stride_b, out_stride_h;
+} nq_attend_params_t;
+
+size_t nq_attend_compressed_workspace_size(int32_t batch, int32_t q_heads, int32_t heads, int32_t n_tokens);
+nq_status_t nq_attend_compressed(const nq_attend_params_t *params, void *workspace, size_t workspace_bytes,
+                                 nq_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

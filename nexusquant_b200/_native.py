@@ -65,6 +65,16 @@ class DecompressParams(ctypes.Structure):
                 ("n_layers", c_i32)]
 
 
+class AttendParams(ctypes.Structure):
+    _fields_ = [("batch", c_i32), ("q_heads", c_i32), ("heads", c_i32), ("head_dim", c_i32),
+                ("head_dim_padded", c_i32), ("n_tokens", c_i32), ("count", c_vp), ("q", c_vp),
+                ("q_stride_b", c_i64), ("q_stride_h", c_i64), ("k_codes", c_vp), ("v_codes", c_vp),
+                ("k_scales", c_vp), ("v_scales", c_vp), ("key_levels", c_i32), ("value_levels", c_i32),
+                ("positions", c_vp), ("rope_cos", c_vp), ("rope_sin", c_vp), ("rope_rows", c_i32),
+                ("key_sharpen", c_f32), ("scale", c_f32), ("out", c_vp), ("out_stride_b", c_i64),
+                ("out_stride_h", c_i64)]
+
+
 # name -> (restype, argtypes)
 _PROTOS = {
     "nq_status_string": (ctypes.c_char_p, [c_i32]),
@@ -86,6 +96,8 @@ _PROTOS = {
     "nq_gather_rows": (c_i32, [c_vp, c_i32, c_i32, c_i32, c_i32, c_i64, c_i64, c_i64, c_vp, c_vp, c_i32, c_vp,
                                c_i64, c_i64, c_i64, c_vp]),
     "nq_delta_codes": (c_i32, [c_vp, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp]),
+    "nq_attend_compressed_workspace_size": (c_size, [c_i32, c_i32, c_i32, c_i32]),
+    "nq_attend_compressed": (c_i32, [ctypes.POINTER(AttendParams), c_vp, c_size, c_vp]),
 }
 
 EXPORTED = tuple(_PROTOS)

@@ -304,3 +304,57 @@ nq_status_t nq_delta_codes(const uint8_t* codes, int32_t n_streams, int32_t n_to
 }
 
 }  // extern "C"
+
+extern "C" {
+size_t nq_attend_compressed_workspace_size(int32_t batch, int32_t q_heads, int32_t heads, int32_t n_tokens) {
+  if (batch <= 0 || q_heads <= 0 || heads <= 0 || n_tokens <= 0) return 0;
+  return nq::attend_workspace_bytes(batch, q_heads, nq::attend_splits(batch, heads, n_tokens));
+}
+
+nq_status_t nq_attend_compressed(const nq_attend_params_t* p, void* workspace, size_t workspace_bytes,
+                                 nq_stream_t stream) {
+  if (!p) return NQ_ERR_INVALID_ARG;
+  if (p->batch < 0 || p->q_heads <= 0 || p->heads <= 0 || p->n_tokens < 0) return NQ_ERR_INVALID_ARG;
+  if (p->head_dim != 128 || p->head_dim_padded != 128) return NQ_ERR_UNSUPPORTED;
+  const int g = p->q_heads % p->heads ? 0 : p->q_heads / p->heads;
+  if (g != 1 && g != 2 && g != 4 && g != 8) return NQ_ERR_UNSUPPORTED;
+  if (!valid_levels(p->key_levels) || !valid_levels(p->value_levels)) return NQ_ERR_INVALID_ARG;
+  if (p->batch == 0) return NQ_OK;
+  if (!p->q || !p->out || !p->k_codes || !p->v_codes || !p->k_scales || !p->v_scales || !p->positions ||
+      !p->rope_cos || !p->rope_sin || p->rope_rows <= 0)
+    return NQ_ERR_INVALID_ARG;
+  const void* al[] = {p->k_codes, p->v_codes, p->rope_cos, p->rope_sin};
+  for (const void* q : al)
+    if (!aligned16(q)) return NQ_ERR_ALIGNMENT;
+  if (p->n_tokens == 0) {
+    // nothing to attend: zero outputs
+    for (int b = 0; b < p->batch; ++b)
+      for (int h = 0; h < p->q_heads; ++h) {
+        const cudaError_t e = cudaMemsetAsync(p->out + b * p->out_stride_b + h * p->out_stride_h, 0, 256,
+                                              static_cast<cudaStream_t>(stream));
+        if (e != cudaSuccess) return NQ_ERR_CUDA;
+      }
+    return NQ_OK;
+  }
+  const int splits = nq::attend_splits(p->batch, p->heads, p->n_tokens);
+  if (!workspace || workspace_bytes < nq::attend_workspace_bytes(p->batch, p->q_heads, splits))
+    return NQ_ERR_WORKSPACE;
+  nq::AttendArgs a{};
+  a.batch = p->batch; a.q_heads = p->q_heads; a.heads = p->heads; a.n_tokens = p->n_tokens;
+  a.splits = splits;
+  const int tiles = (p->n_tokens + 127) / 128;
+  a.tokens_per_split = ((tiles + splits - 1) / splits) * 128;
+  a.count = p->count;
+  a.q = reinterpret_cast<const __half*>(p->q);
+  a.q_stride_b = p->q_stride_b; a.q_stride_h = p->q_stride_h;
+  a.k_codes = p->k_codes; a.v_codes = p->v_codes; a.k_scales = p->k_scales; a.v_scales = p->v_scales;
+  a.positions = p->positions; a.rope_cos = p->rope_cos; a.rope_sin = p->rope_sin;
+  a.key_sharpen = p->key_sharpen == 0.0f ? 1.0f : p->key_sharpen;
+  a.scale = p->scale == 0.0f ? 1.0f / sqrtf((float)p->head_dim) : p->scale;
+  a.out = reinterpret_cast<__half*>(p->out);
+  a.out_stride_b = p->out_stride_b; a.out_stride_h = p->out_stride_h;
+  auto fmt = [](int levels) { return levels <= 4 ? 0 : (levels == 8 ? 1 : 2); };
+  return cuda_status(nq::launch_attend(a, fmt(p->key_levels), fmt(p->value_levels), workspace,
+                                       static_cast<cudaStream_t>(stream)));
+}
+}  // extern "C"

@@ -1,5 +1,6 @@
 // Internal (non-ABI) declarations shared by the kernels and the C entry points.
 #pragma once
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -103,5 +104,29 @@ cudaError_t launch_gather_rows(const void* in, int dtype, int batch, int heads, 
                                int n_kept, uint16_t* out, int64_t osb, int64_t osh, int64_t ost, cudaStream_t s);
 cudaError_t launch_delta(const uint8_t* codes, int n_streams, int n_tokens, int dp, int levels, int8_t* delta,
                          cudaStream_t s);
+
+// compressed-domain decode attention (nq_attend.cu)
+struct AttendArgs {
+  int32_t batch, q_heads, heads, n_tokens, splits, tokens_per_split;
+  const int32_t* count;
+  const __half* q;
+  int64_t q_stride_b, q_stride_h;
+  const uint8_t* k_codes;
+  const uint8_t* v_codes;
+  const uint16_t* k_scales;
+  const uint16_t* v_scales;
+  const int32_t* positions;
+  const float* rope_cos;
+  const float* rope_sin;
+  float key_sharpen, scale;
+  float* ws_m;    // [b, hq, splits]
+  float* ws_l;    // [b, hq, splits]
+  float* ws_acc;  // [b, hq, splits, 128]
+  __half* out;
+  int64_t out_stride_b, out_stride_h;
+};
+int attend_splits(int batch, int heads, int n_tokens);
+size_t attend_workspace_bytes(int batch, int q_heads, int splits);
+cudaError_t launch_attend(const AttendArgs& a, int fmt_k, int fmt_v, void* ws, cudaStream_t s);
 
 }  // namespace nq

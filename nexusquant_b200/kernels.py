@@ -402,3 +402,44 @@ def e8_quantize_perhead(x: torch.Tensor, levels: int = 4) -> torch.Tensor:
     compress_layers([None], [rows], key_levels=levels, value_levels=levels, emit_codes=False, recon_v=[out],
                     rotate=False)
     return out.reshape(*lead, d)
+
+
+def attend_compressed(q: torch.Tensor, codes: LayerCodes, positions: torch.Tensor, *,
+                      count: Optional[torch.Tensor] = None, rope_base: float = 10000.0,
+                      rope_scaling: Optional[dict] = None, key_sharpen: float = 1.0,
+                      scale: Optional[float] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Decode attention over one compressed layer (NexusQuantPagedAttention.forward,
+    vllm_backend.py:692-765) without materialising fp16 K/V.
+
+    q         : fp16 [b, hq, 128], one query token per sequence (RoPE already applied).
+    codes     : LayerCodes of the layer ([b, h, n, pb] codes, [b, h, n] fp16 scales); hq / h in {1,2,4,8}.
+    positions : int32 [b, n] RoPE positions of the stored keys.
+    Returns fp16 [b, hq, 128] = softmax(q K^T * scale) V with K, V as decompress_layers gives them."""
+    _require_cuda(q, positions, count)
+    b, hq, d = q.shape
+    _, h, n, _ = codes.k_codes.shape
+    dev = q.device
+    if q.dtype != torch.float16:
+        raise TypeError("query must be fp16")
+    q = q if q.stride(-1) == 1 else q.contiguous()
+    positions = positions.to(device=dev, dtype=torch.int32).contiguous()
+    if count is not None:
+        count = count.to(device=dev, dtype=torch.int32).contiguous()
+    rows = int(positions.max().item()) + 1 if positions.numel() else 1
+    cos, sin = TABLES.get(dev, d, rope_base, rows, rope_scaling)
+    if out is None:
+        out = torch.empty((b, hq, d), dtype=torch.float16, device=dev)
+    ws = _workspace(dev, N.load().nq_attend_compressed_workspace_size(b, hq, h, n))
+    p = N.AttendParams()
+    p.batch, p.q_heads, p.heads, p.head_dim, p.head_dim_padded, p.n_tokens = b, hq, h, d, next_pow2(d), n
+    p.count, p.q = _ptr(count), q.data_ptr()
+    p.q_stride_b, p.q_stride_h = q.stride(0), q.stride(1)
+    p.k_codes, p.v_codes = codes.k_codes.data_ptr(), codes.v_codes.data_ptr()
+    p.k_scales, p.v_scales = codes.k_scales.data_ptr(), codes.v_scales.data_ptr()
+    p.key_levels, p.value_levels = codes.key_levels, codes.value_levels
+    p.positions, p.rope_cos, p.rope_sin, p.rope_rows = positions.data_ptr(), cos.data_ptr(), sin.data_ptr(), cos.shape[0]
+    p.key_sharpen = float(key_sharpen)
+    p.scale = 0.0 if scale is None else float(scale)
+    p.out, p.out_stride_b, p.out_stride_h = out.data_ptr(), out.stride(0), out.stride(1)
+    N.call("nq_attend_compressed", ctypes.byref(p), ws.data_ptr(), ws.numel(), _stream(dev))
+    return out

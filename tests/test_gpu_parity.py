@@ -317,3 +317,38 @@ def test_host_resident_inputs_match_device(orc):
         N.call("nq_gather_rows", k.data_ptr(), 0, 2, 4, 128, *k.stride()[:3], kept.data_ptr(), None, 111,
                torch.empty((2, 4, 111, 128), dtype=torch.float16, device=DEV).data_ptr(), 4 * 111 * 128,
                111 * 128, 128, None)
+
+
+def _attend_ref(q, ok, ov, count, scale):
+    """NexusQuantPagedAttention.forward restated in torch (fp32 softmax over fp16 K/V)."""
+    b, hq, d = q.shape
+    h = ok.shape[1]
+    out = torch.zeros_like(q)
+    for bi in range(b):
+        n = int(count[bi])
+        if n == 0:
+            continue
+        k = ok[bi, :, :n].float().repeat_interleave(hq // h, 0)
+        v = ov[bi, :, :n].float().repeat_interleave(hq // h, 0)
+        w = torch.softmax(torch.einsum("hd,hnd->hn", q[bi].float(), k) * scale, -1)
+        out[bi] = torch.einsum("hn,hnd->hd", w, v).to(torch.float16)
+    return out
+
+
+@pytest.mark.parametrize("lk,lv,g,sharpen", [(4, 4, 1, 1.0), (8, 4, 2, K.SHARPEN), (16, 16, 4, 1.0), (2, 8, 8, 1.0)])
+def test_attend_compressed_vs_decompress_then_attention(orc, lk, lv, g, sharpen):
+    """Decode attention over the compressed layout equals dequantize + the reference attention."""
+    cfg = syn.CacheConfig("t", 1, 2, 2, 700, 128)
+    k, v = syn.cpu_layer(cfg, 6)
+    rng = np.random.default_rng(lk + g)
+    kept = np.stack([np.sort(rng.choice(700, 333, replace=False)) for _ in range(2)])
+    lc = _run_compress(k, v, kept, lk, lv)
+    pos = torch.as_tensor(kept, dtype=torch.int32, device=DEV)
+    count = torch.tensor([333, 150], dtype=torch.int32, device=DEV)  # ragged second sequence
+    ok, ov = K.decompress_layers([lc], pos, head_dim=128, count=count, key_sharpen=sharpen)
+    q = (torch.randn(2, 2 * g, 128, generator=torch.Generator().manual_seed(g)) * 0.3).to(torch.float16).to(DEV)
+    got = K.attend_compressed(q, lc, pos, count=count, key_sharpen=sharpen)
+    ref = _attend_ref(q, ok[0], ov[0], count.cpu(), 128 ** -0.5)
+    assert rel_l2(got.cpu().numpy(), ref.cpu().numpy()) < REL_L2_TOL
+    again = K.attend_compressed(q, lc, pos, count=count, key_sharpen=sharpen)
+    assert torch.equal(got, again)  # deterministic
