@@ -174,7 +174,7 @@ class Shard:
                               key_levels=self.levels[0], value_levels=self.levels[1], kept_idx=idx[:, :self.cap],
                               kept_count=cnt, n_kept=self.cap, rope_base=cfg.rope_base, rope_rows=T,
                               codes_out=self.codes)
-            self.launches += math.ceil(len(self.quant) / 96)
+            self.launches += 2 * math.ceil(len(self.quant) / 96)  # key and value kernels
         for l in self.prot:
             K.gather_rows(self.K[l], idx[:, :self.cap], self.cap, cnt, out=self.prot_out[l][0])
             K.gather_rows(self.V[l], idx[:, :self.cap], self.cap, cnt, out=self.prot_out[l][1])

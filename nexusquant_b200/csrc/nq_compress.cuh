@@ -570,17 +570,21 @@ __device__ __forceinline__ void compress_tile(const CompressArgs& a, const Tile&
 }
 
 // --------------------------------------------------------------------------
-// Persistent kernel: 1- or 2-stage cp.async pipeline over the tile list.
+// Persistent kernel: 1- or 2-stage cp.async pipeline over the tile list.  KVS selects the
+// key tiles (0, the first half of the tile list) or the value tiles (1): each instantiation
+// holds one per-vector body, half the code of a kernel that handles both, which keeps the
+// instruction cache from thrashing.
 // --------------------------------------------------------------------------
-template <typename TIn, int D, int DP, int FMTK, int FMTV, bool RECON>
+template <typename TIn, int D, int DP, int FMTK, int FMTV, bool RECON, int KVS>
 __global__ void __launch_bounds__(kCompressThreads, 4) compress_kernel(const CompressArgs args, int n_layers,
                                                                         int n_tiles, int ns) {
   using S = Smem<TIn, D>;
   extern __shared__ __align__(128) uint8_t smem[];
   const int first = blockIdx.x;
   if (first >= n_tiles) return;
+  const int base = KVS * n_tiles;  // n_tiles = tiles of this half
   const int stage_bytes = S::stage(args.head_group);
-  Tile cur = decode_tile(args, n_layers, first);
+  Tile cur = decode_tile(args, n_layers, base + first);
   issue_tile<TIn, D>(args, cur, smem);
   cp_async_commit();
   int it = 0;
@@ -591,7 +595,7 @@ __global__ void __launch_bounds__(kCompressThreads, 4) compress_kernel(const Com
     const int next = tile + (int)gridDim.x;
     const bool has_next = next < n_tiles;
     Tile nt = cur;
-    if (has_next) nt = decode_tile(args, n_layers, next);
+    if (has_next) nt = decode_tile(args, n_layers, base + next);
     if (ns == 2) {
       __syncwarp();  // this warp is done with stage s^1 (previous tile)
       if (has_next) issue_tile<TIn, D>(args, nt, smem + (s ^ 1) * stage_bytes);
@@ -602,7 +606,7 @@ __global__ void __launch_bounds__(kCompressThreads, 4) compress_kernel(const Com
     }
     __syncwarp();
     const uint8_t* stage = smem + s * stage_bytes;
-    if (cur.kv == 0) compress_tile<TIn, D, DP, true, FMTK, RECON>(args, cur, stage);
+    if constexpr (KVS == 0) compress_tile<TIn, D, DP, true, FMTK, RECON>(args, cur, stage);
     else compress_tile<TIn, D, DP, false, FMTV, RECON>(args, cur, stage);
     if (ns == 1 && has_next) {
       __syncwarp();
@@ -625,15 +629,23 @@ static cudaError_t launch_fmt(const CompressArgs& a, int n_layers, long long n_t
   if ((e = cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess) return e;
   const int ns = 2 * (size_t)S::stage(a.head_group) + 64 <= (size_t)max_smem ? 2 : 1;
   const size_t smem = ns * (size_t)S::stage(a.head_group);
-  auto kern = recon ? compress_kernel<TIn, D, DP, FMTK, FMTV, true> : compress_kernel<TIn, D, DP, FMTK, FMTV, false>;
-  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
-  if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
-  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kCompressThreads, smem)) != cudaSuccess)
-    return e;
-  long long grid = (long long)sms * (per_sm > 0 ? per_sm : 1);
-  if (grid > n_tiles) grid = n_tiles;
-  kern<<<(unsigned)grid, kCompressThreads, smem, s>>>(a, n_layers, n_tiles, ns);
+  // key tiles (first half of the tile list), then value tiles, one kernel each
+  const long long half = n_tiles / 2;
+  for (int kvs = 0; kvs < 2; ++kvs) {
+    auto kern = kvs == 0 ? (recon ? compress_kernel<TIn, D, DP, FMTK, FMTV, true, 0>
+                                  : compress_kernel<TIn, D, DP, FMTK, FMTV, false, 0>)
+                         : (recon ? compress_kernel<TIn, D, DP, FMTK, FMTV, true, 1>
+                                  : compress_kernel<TIn, D, DP, FMTK, FMTV, false, 1>);
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kCompressThreads, smem)) != cudaSuccess)
+      return e;
+    long long grid = (long long)sms * (per_sm > 0 ? per_sm : 1);
+    if (grid > half) grid = half;
+    if (grid > 0) kern<<<(unsigned)grid, kCompressThreads, smem, s>>>(a, n_layers, (int)half, ns);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
   return cudaGetLastError();
 }
 
