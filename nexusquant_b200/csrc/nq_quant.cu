@@ -242,7 +242,9 @@ __device__ __forceinline__ void decompress_vector(const DecompressArgs& args, co
   finish_store<D, DP, KEY, V8>(R, coef, trow, trow + DH, args.key_sharpen, o);
 }
 
-template <int D, int DP, bool V8>
+// KEY: this launch covers the key rows (true) or the value rows (false) of every layer; one
+// half per kernel keeps each kernel's code (three packing formats) small for the i-cache.
+template <int D, int DP, bool V8, bool KEY>
 __global__ void __launch_bounds__(kCompressThreads, 4) decompress_kernel(const DecompressArgs args) {
   extern __shared__ __align__(16) uint8_t rope_smem[];
   const int HG = args.head_group;
@@ -253,36 +255,30 @@ __global__ void __launch_bounds__(kCompressThreads, 4) decompress_kernel(const D
   const int tt = bid % t_tiles; bid /= t_tiles;
   const int hg = bid % h_groups; bid /= h_groups;
   const int b = bid % args.batch; bid /= args.batch;
-  const int kv = bid & 1;
-  const int layer = bid >> 1;
+  const int layer = bid;
   const DLayerIO& L = args.layers[layer];
-  const bool key = kv == 0;
-  if ((key ? L.k_codes : L.v_codes) == nullptr) return;
+  if ((KEY ? L.k_codes : L.v_codes) == nullptr) return;
   const int j = tt * TOK + threadIdx.x / HG;
   const int head = hg * HG + threadIdx.x % HG;
   const int count = args.count ? min(args.count[b], args.n_tokens) : args.n_tokens;
   // invalid threads stay until the warp-level barrier of the key path
   const bool valid = j < count && head < args.heads;
-  const int levels = key ? L.key_levels : L.value_levels;
+  const int levels = KEY ? L.key_levels : L.value_levels;
   const int fmt = levels <= 4 ? 0 : (levels == 8 ? 1 : 2);
-  if (key) {
-    if (fmt == 0) decompress_vector<D, DP, true, 0, V8>(args, L, b, head, j, valid, rope_smem);
-    else if (fmt == 1) decompress_vector<D, DP, true, 1, V8>(args, L, b, head, j, valid, rope_smem);
-    else decompress_vector<D, DP, true, 2, V8>(args, L, b, head, j, valid, rope_smem);
-  } else {
-    if (fmt == 0) decompress_vector<D, DP, false, 0, V8>(args, L, b, head, j, valid, rope_smem);
-    else if (fmt == 1) decompress_vector<D, DP, false, 1, V8>(args, L, b, head, j, valid, rope_smem);
-    else decompress_vector<D, DP, false, 2, V8>(args, L, b, head, j, valid, rope_smem);
-  }
+  if (fmt == 0) decompress_vector<D, DP, KEY, 0, V8>(args, L, b, head, j, valid, rope_smem);
+  else if (fmt == 1) decompress_vector<D, DP, KEY, 1, V8>(args, L, b, head, j, valid, rope_smem);
+  else decompress_vector<D, DP, KEY, 2, V8>(args, L, b, head, j, valid, rope_smem);
 }
 
 template <int D, int DP, bool V8>
 static cudaError_t launch_dq_t(const DecompressArgs& a, long long blocks, cudaStream_t s) {
   const int smem = (kCompressThreads / a.head_group) * RopeSmem<D>::kRow;
   cudaError_t e =
-      cudaFuncSetAttribute(decompress_kernel<D, DP, V8>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      cudaFuncSetAttribute(decompress_kernel<D, DP, V8, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  decompress_kernel<D, DP, V8><<<(int)blocks, kCompressThreads, smem, s>>>(a);
+  decompress_kernel<D, DP, V8, true><<<(int)blocks, kCompressThreads, smem, s>>>(a);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  decompress_kernel<D, DP, V8, false><<<(int)blocks, kCompressThreads, 0, s>>>(a);  // values: no RoPE rows
   return cudaGetLastError();
 }
 
@@ -307,7 +303,7 @@ static cudaError_t launch_dq(const DecompressArgs& a, int n_layers, long long bl
 // --------------------------------------------------------------------------
 cudaError_t launch_decompress(const DecompressArgs& a, int n_layers, cudaStream_t s) {
   const int tok = kCompressThreads / a.head_group;
-  const long long blocks = (long long)n_layers * 2 * a.batch * ((a.heads + a.head_group - 1) / a.head_group) *
+  const long long blocks = (long long)n_layers * a.batch * ((a.heads + a.head_group - 1) / a.head_group) *
                            ((a.n_tokens + tok - 1) / tok);
   if (blocks <= 0) return cudaSuccess;
   if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;

@@ -2,7 +2,8 @@
 // BOS + last `sliding_window` tokens + top-n_keep of importance[1:prefix]
 // + protected positions, emitted as ascending token indices.
 //
-// One thread-block cluster of kSelCtas CTAs (1024 threads each) per batch row;
+// One thread-block cluster of 16 CTAs (1024 threads each; 8 for short rows or where
+// clusters of 16 are not available) per batch row;
 // CTA c owns the c-th slice of the row.  Every pass reads the row with
 // coalesced 16-byte loads (after the first pass they hit L2).
 //  1. MSB-first radix select of the k-th largest order-preserving key over 3
@@ -25,7 +26,6 @@ namespace nq {
 constexpr int kSelThreads = 1024;
 constexpr int kSelWarps = kSelThreads / 32;
 constexpr int kSelChunk = kSelThreads * 4;
-constexpr int kSelCtas = 8;  // CTAs per row (one cluster)
 
 // Order-preserving unsigned key; -0.0 and +0.0 compare equal (one tie class), as in a float compare.
 __device__ __forceinline__ uint32_t order_key(float f) {
@@ -137,23 +137,25 @@ __device__ __forceinline__ int compact_slice(const float* x, int seq, int sw, in
   return count;
 }
 
-__global__ void __cluster_dims__(kSelCtas, 1, 1) __launch_bounds__(kSelThreads)
+// CS CTAs per row form one thread-block cluster (set at launch).
+template <int CS>
+__global__ void __launch_bounds__(kSelThreads)
     select_kernel(const float* imp, int seq, int sw, int n_keep, const int32_t* prot, int n_prot, int32_t* kept_idx,
                   int32_t* kept_count) {
   __shared__ uint32_t hist[2048];   // this CTA's histogram
   __shared__ uint32_t ghist[2048];  // CTA 0: the cluster's histogram
   __shared__ uint32_t s_pref, s_rem;
   __shared__ int scan_sh[32];
-  __shared__ int cnt_keep[kSelCtas], cnt_tie[kSelCtas];  // CTA 0: per-slice counts
+  __shared__ int cnt_keep[CS], cnt_tie[CS];  // CTA 0: per-slice counts
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = (int)cluster.block_rank();
-  const int b = blockIdx.x / kSelCtas;
+  const int b = blockIdx.x / CS;
   const float* x = imp + (int64_t)b * seq;
   const int prefix = max(seq - sw, 0);
   const int k = (prefix > 1 && n_keep > 0) ? min(n_keep, prefix - 1) : 0;
   const int lane = threadIdx.x & 31;
   // this CTA's slice [lo, hi), a multiple of 4 tokens wide
-  const int per = ((seq + kSelCtas - 1) / kSelCtas + 3) & ~3;
+  const int per = ((seq + CS - 1) / CS + 3) & ~3;
   const int lo = min(seq, rank * per), hi = min(seq, lo + per);
   uint32_t* g0 = cluster.map_shared_rank(ghist, 0);
   uint32_t* pref0 = cluster.map_shared_rank(&s_pref, 0);
@@ -271,7 +273,7 @@ __global__ void __cluster_dims__(kSelCtas, 1, 1) __launch_bounds__(kSelThreads)
   {
     const int* ck = cluster.map_shared_rank(cnt_keep, 0);
     int total = 0;
-    for (int r = 0; r < kSelCtas; ++r) {
+    for (int r = 0; r < CS; ++r) {
       if (r == rank) out_base = total;
       total += ck[r];
     }
@@ -284,11 +286,53 @@ __global__ void __cluster_dims__(kSelCtas, 1, 1) __launch_bounds__(kSelThreads)
 
 size_t select_workspace_bytes(int, int) { return 0; }
 
+template <int CS>
+static cudaError_t launch_cs(const float* imp, int batch, int seq, int sw, int n_keep, const int32_t* prot,
+                             int n_prot, int32_t* kept_idx, int32_t* kept_count, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(batch * CS);
+  cfg.blockDim = dim3(kSelThreads);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CS;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, select_kernel<CS>, imp, seq, sw, n_keep, prot, n_prot, kept_idx, kept_count);
+}
+
+// 16 CTAs per row where the device schedules clusters of 16 (a non-portable size), else 8.
+static bool cluster16_ok() {
+  static int ok = -1;
+  if (ok < 0) {
+    ok = 0;
+    if (cudaFuncSetAttribute(select_kernel<16>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(16);
+      cfg.blockDim = dim3(kSelThreads);
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 16;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int clusters = 0;
+      if (cudaOccupancyMaxActiveClusters(&clusters, select_kernel<16>, &cfg) == cudaSuccess && clusters > 0) ok = 1;
+    }
+    cudaGetLastError();
+  }
+  return ok == 1;
+}
+
 cudaError_t launch_select(const float* imp, int batch, int seq, int sw, int n_keep, const int32_t* prot, int n_prot,
                           int32_t* kept_idx, int32_t* kept_count, void*, cudaStream_t s) {
   if (batch == 0) return cudaSuccess;
-  select_kernel<<<batch * kSelCtas, kSelThreads, 0, s>>>(imp, seq, sw, n_keep, prot, n_prot, kept_idx, kept_count);
-  return cudaGetLastError();
+  if (seq >= 16 * kSelChunk && cluster16_ok())
+    return launch_cs<16>(imp, batch, seq, sw, n_keep, prot, n_prot, kept_idx, kept_count, s);
+  return launch_cs<8>(imp, batch, seq, sw, n_keep, prot, n_prot, kept_idx, kept_count, s);
 }
 
 }  // namespace nq
