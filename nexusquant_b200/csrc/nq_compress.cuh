@@ -475,7 +475,6 @@ __device__ __forceinline__ void compress_tile(const CompressArgs& a, const Tile&
   const float sc = __fmul_rn(amax, 2.0f / static_cast<float>(levels));
   const float rcp = __frcp_rn(sc);
   const u64 r2 = pk(rcp, rcp), nsc2 = pk(-sc, -sc);
-  const u64 M2 = pk(kMagic, kMagic), half2 = pk(0.5f, 0.5f);
 
   // ---- lattice: this thread's groups g (low lanes) and g + DP/16 (high lanes)
   constexpr int GT = HP / 8;                  // groups per lane type per thread
@@ -497,13 +496,14 @@ __device__ __forceinline__ void compress_tile(const CompressArgs& a, const Tile&
       const u64 q1 = mul2(y, r2);
       const u64 rem = fma2(q1, nsc2, y);
       const u64 n = fma2(rem, r2, q1);
-      const u64 s = add2(n, M2);
-      const u64 e = sub2(n, sub2(s, M2));
-      const u64 sb = add2(sub2(n, half2), M2);
-      float s0, s1, b0, b1;
-      upk(e, elo[i], ehi[i]);
-      upk(s, s0, s1);
-      upk(sb, b0, b1);
+      // the roundings run as scalar fp32 ops: unlike the packed ones they can issue to
+      // either FMA pipe, which balances the pipes here (measured ~4 % faster)
+      float n0, n1;
+      upk(n, n0, n1);
+      const float s0 = __fadd_rn(n0, kMagic), s1 = __fadd_rn(n1, kMagic);
+      elo[i] = __fsub_rn(n0, __fsub_rn(s0, kMagic));
+      ehi[i] = __fsub_rn(n1, __fsub_rn(s1, kMagic));
+      const float b0 = __fadd_rn(__fsub_rn(n0, 0.5f), kMagic), b1 = __fadd_rn(__fsub_rn(n1, 0.5f), kMagic);
       slo[i] = __float_as_uint(s0); shi[i] = __float_as_uint(s1);
       blo[i] = __float_as_uint(b0); bhi[i] = __float_as_uint(b1);
     }
