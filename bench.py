@@ -160,6 +160,9 @@ class Shard:
     def step(self):
         cfg = self.cfg
         b, h, T = cfg.batch, cfg.heads, cfg.seq
+        # global index of the compressed cache: the per-layer byte sizes of fixed-capacity
+        # outputs are known up front, so their exchange overlaps scoring and compression
+        _, sizes_work = S.gather_layer_index(self.sizes, self.plan, self.group, self.sizes_all, async_op=True)
         if self.h1 > self.h0:
             ph = K.score_keykey(self.K0, 32, head_range=(self.h0, self.h1), per_head=True)
             self.launches += 3
@@ -180,9 +183,8 @@ class Shard:
             K.gather_rows(self.V[l], idx[:, :self.cap], self.cap, cnt, out=self.prot_out[l][1])
             self.launches += 2
         self.kept_idx, self.kept_count = idx, cnt
-        if self.world > 1:
-            # global index of the compressed cache: per-layer byte sizes from every rank
-            S.gather_layer_index(self.sizes, self.plan, self.group, self.sizes_all)
+        if sizes_work is not None:
+            sizes_work.wait()
 
     def compress_only(self):
         K.compress_layers([self.K[l] for l in self.quant], [self.V[l] for l in self.quant],
@@ -312,6 +314,7 @@ def e2e_leg(sh: Shard, steps: int, group_layers: int = 8):
     groups = [sh.quant[i:i + group_layers] for i in range(0, len(sh.quant), group_layers)]
 
     def step():
+        _, sizes_work = S.gather_layer_index(sh.sizes, sh.plan, sh.group, sh.sizes_all, async_op=True)
         if sh.h1 > sh.h0:
             k0_dev[:, sh.h0:sh.h1].copy_(host_k0[:, sh.h0:sh.h1], non_blocking=True)
             ph = K.score_keykey(k0_dev, 32, head_range=(sh.h0, sh.h1), per_head=True)
@@ -344,8 +347,8 @@ def e2e_leg(sh: Shard, steps: int, group_layers: int = 8):
             with torch.cuda.stream(dn):
                 prot_host[l][0].copy_(sh.prot_out[l][0], non_blocking=True)
                 prot_host[l][1].copy_(sh.prot_out[l][1], non_blocking=True)
-        if sh.world > 1:
-            S.gather_layer_index(sh.sizes, sh.plan, sh.group, sh.sizes_all)
+        if sizes_work is not None:
+            sizes_work.wait()
         done = torch.cuda.Event()
         done.record(dn)
         comp.wait_event(done)

@@ -123,14 +123,19 @@ def local_layer_sizes(plan: ShardPlan, compressed_bytes: Sequence[int], protecte
 
 
 def gather_layer_index(sizes: torch.Tensor, plan: ShardPlan, group=None,
-                       sizes_all: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """All-gather per-layer sizes -> int64 [world, n_layers] (row r = rank r's sizes)."""
+                       sizes_all: Optional[torch.Tensor] = None, async_op: bool = False):
+    """All-gather per-layer sizes -> int64 [world, n_layers] (row r = rank r's sizes).
+    async_op=True returns (table, work): with fixed-capacity outputs the sizes are known before
+    the layers are compressed, so the exchange can run while they are; call work.wait()
+    (work is None on one rank) before reading the table."""
     if plan.world == 1:
-        return sizes.reshape(1, -1)
+        table = sizes.reshape(1, -1)
+        return (table, None) if async_op else table
     if sizes_all is None:
         sizes_all = torch.empty((plan.world * sizes.numel(),), dtype=torch.int64, device=sizes.device)
-    dist.all_gather_into_tensor(sizes_all.view(-1), sizes.view(-1), group=group)
-    return sizes_all.view(plan.world, -1)
+    work = dist.all_gather_into_tensor(sizes_all.view(-1), sizes.view(-1), group=group, async_op=async_op)
+    table = sizes_all.view(plan.world, -1)
+    return (table, work) if async_op else table
 
 
 def layer_owners(assignment: Sequence[Sequence[int]], n_layers: int) -> List[int]:

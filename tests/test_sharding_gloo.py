@@ -69,6 +69,10 @@ def _worker(rank, world, port, q):
         prot = [50000 + l for l in plan.protected]
         sizes = S.local_layer_sizes(plan, comp, prot)
         sizes_all = S.gather_layer_index(sizes, plan)
+        table_async, work = S.gather_layer_index(sizes, plan, async_op=True)
+        if work is not None:
+            work.wait()
+        assert torch.equal(table_async, sizes_all)
         owners = S.layer_owners(S.assign_layers(L, S.protected_layers(L, PB), world), L)
         table = S.layer_table(sizes_all, owners)
         prot_set = S.protected_layers(L, PB)
