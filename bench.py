@@ -469,9 +469,11 @@ def main():
                        "kept_tokens": sh.cap, "protected_layers": sorted(sh.protected),
                        "parallelism": f"layer-sharded x{world}", "l2": f"inputs ({cfg.fp16_bytes / 1e9:.2f} GB) larger than L2; no flush"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
+                         "frac": round(achieved / peak, 4), "frac_of_spec_8tbs": round(achieved / 8000.0, 4),
+                         "traffic": traffic, "peak_kind": peak_kind,
                          "kernel": "compress_kernel", "launch_ms": round(kms, 4), "algo_bytes": algo},
             "dequant": {"value": round(dq_achieved, 1), "unit": "GB/s", "frac": round(dq_achieved / peak, 4),
+                        "frac_of_spec_8tbs": round(dq_achieved / 8000.0, 4),
                         "launch_ms": round(dms, 4), "algo_bytes": dq_bytes},
             "cpu_baseline": cpu,
             "e2e": e2e if e2e is not None else {"value": None, "unit": "GB/s", "error": e2e_err},
