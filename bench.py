@@ -273,10 +273,10 @@ def cpu_sample(cfg, seconds_hint: float = 15.0):
 def e2e_leg(sh: Shard, steps: int, group_layers: int = 8):
     """End to end through the public API with the cache in pinned host memory.  Per step:
     layer 0's keys of this rank's heads are copied host->device for scoring; the keep set is
-    selected on the device; the compress kernels then read only the kept rows of each layer
-    straight from host memory (mapped, over PCIe), a group of layers per launch, and each
-    group's codes and scales are copied device->host on a second stream while the next group
-    is read; protected layers' kept rows are gathered from host memory the same way."""
+    selected on the device; for each group of layers a gather kernel reads only the kept rows
+    from host memory (mapped, over PCIe) into device memory and the compress kernel encodes
+    them there, and each group's codes and scales are copied device->host on a second stream
+    while the next group is read; protected layers' kept rows are gathered the same way."""
     cfg = sh.cfg
     dev = sh.dev
     try:
@@ -359,7 +359,7 @@ def e2e_leg(sh: Shard, steps: int, group_layers: int = 8):
     return {"value": round(cfg.fp16_bytes * steps / (ms / 1e3) / 1e9, 3), "unit": "GB/s",
             "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": steps,
             "ms_per_step": round(ms / steps, 3),
-            "path": "cache in pinned host memory; kernels read the kept rows across PCIe"}, None
+            "path": "cache in pinned host memory; a gather kernel reads the kept rows across PCIe, then compress"}, None
 
 
 # ------------------------------------------------------------------- reference

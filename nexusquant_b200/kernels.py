@@ -86,7 +86,8 @@ def compress_layers(ks: Sequence[Optional[torch.Tensor]], vs: Sequence[Optional[
                     recon_rows: str = "source", recon_positions: Optional[torch.Tensor] = None,
                     key_sharpen: float = 1.0, rope_rows: Optional[int] = None,
                     codes_out: Optional[Sequence[LayerCodes]] = None, rotate: bool = True,
-                    device: Optional[torch.device] = None) -> List[LayerCodes]:
+                    device: Optional[torch.device] = None, stage_host_rows: bool = True,
+                    _rows_known: bool = False) -> List[LayerCodes]:
     """Compress several layers that share one keep set in a single kernel launch.
 
     ks / vs   : per-layer [b, h, T, d] tensors (same shape, dtype, strides); None skips that half.
@@ -96,6 +97,11 @@ def compress_layers(ks: Sequence[Optional[torch.Tensor]], vs: Sequence[Optional[
                 source index (recon_rows="source", masked layout) or j (recon_rows="kept",
                 truncated layout, keys re-encoded at position j unless recon_positions given).
     codes_out : optional preallocated outputs (LayerCodes per layer) to write into.
+    stage_host_rows : with fp16 layers in pinned host memory, a keep set and no reconstruction
+                outputs, first gather the kept rows into device memory (``gather_rows``) and
+                compress them from there with the kept indices as RoPE positions.  The codes
+                are identical; the gather reads the scattered rows across PCIe about twice as
+                fast as the compress kernel does.  False reads them inside the compress kernel.
     Returns one LayerCodes per layer.
     """
     L = len(ks)
@@ -114,6 +120,13 @@ def compress_layers(ks: Sequence[Optional[torch.Tensor]], vs: Sequence[Optional[
         _require_cuda(ref)
         dev = ref.device
     _require_cuda(kept_idx, kept_count, positions)
+    if (host_in and stage_host_rows and kept_idx is not None and ref.dtype == torch.float16
+            and recon_k is None and recon_v is None):
+        return _compress_host_staged(ks, vs, dev, key_levels=key_levels, value_levels=value_levels,
+                                     kept_idx=kept_idx, kept_count=kept_count, positions=positions,
+                                     rope_base=rope_base, rope_scaling=rope_scaling, emit_codes=emit_codes,
+                                     emit_scales_f32=emit_scales_f32, key_sharpen=key_sharpen,
+                                     rope_rows=rope_rows, codes_out=codes_out, rotate=rotate)
     b, h, T, d = ref.shape
     if ref.dtype not in _DTYPES:
         raise TypeError(f"unsupported cache dtype {ref.dtype}")
@@ -139,7 +152,7 @@ def compress_layers(ks: Sequence[Optional[torch.Tensor]], vs: Sequence[Optional[
             raise ValueError("all layers of one compress call must share shape, dtype and strides")
     any_key = any(t is not None for t in ks)
     rows_needed = rope_rows or T
-    if positions is not None and positions.numel():
+    if positions is not None and positions.numel() and not _rows_known:
         rows_needed = max(rows_needed, int(positions.max().item()) + 1)
     cos = sin = None
     if any_key:
@@ -200,6 +213,64 @@ def compress_layers(ks: Sequence[Optional[torch.Tensor]], vs: Sequence[Optional[
     p.layers = ctypes.cast(arr, ctypes.POINTER(N.LayerIO))
     p.n_layers = L
     N.call("nq_compress_layers", ctypes.byref(p), _stream(dev))
+    return outs
+
+
+_STAGE = {}
+_STAGE_LIMIT = 2 << 30  # bytes of staged rows per compress launch
+
+
+def _stage_buffer(dev: torch.device, nelem: int) -> torch.Tensor:
+    """fp16 staging buffer for kept rows, one per (device, stream): calls on one stream are
+    ordered, so reuse across them is safe."""
+    key = (str(dev), torch.cuda.current_stream(dev).cuda_stream)
+    cur = _STAGE.get(key)
+    if cur is None or cur.numel() < nelem:
+        _STAGE.pop(key, None)
+        cur = torch.empty(nelem, dtype=torch.float16, device=dev)
+        _STAGE[key] = cur
+    return cur
+
+
+def _compress_host_staged(ks, vs, dev, *, key_levels, value_levels, kept_idx, kept_count, positions, rope_base,
+                          rope_scaling, emit_codes, emit_scales_f32, key_sharpen, rope_rows, codes_out,
+                          rotate) -> List[LayerCodes]:
+    """Host-resident fp16 layers: gather each layer's kept rows into device memory, then
+    compress the gathered rows (kept index j, RoPE position kept_idx[b, j] unless positions
+    are given).  Layers go in chunks of at most _STAGE_LIMIT staged bytes."""
+    L = len(ks)
+    ref = next(t for t in list(ks) + list(vs) if t is not None)
+    b, h, T, d = ref.shape
+    kept_idx = kept_idx.to(device=dev, dtype=torch.int32).contiguous()
+    n_kept = kept_idx.shape[1]
+    if kept_count is not None:
+        kept_count = kept_count.to(device=dev, dtype=torch.int32).contiguous()
+    rows_known = positions is None  # kept indices are below T, like the unstaged path assumes
+    pos = kept_idx if positions is None else positions
+    klv, vlv = _levels_list(key_levels, L), _levels_list(value_levels, L)
+    per_layer = b * h * n_kept * d
+    halves = [(k is not None) + (v is not None) for k, v in zip(ks, vs)]
+    chunk = max(1, _STAGE_LIMIT // max(1, 2 * 2 * per_layer))
+    outs: List[LayerCodes] = []
+    for l0 in range(0, L, chunk):
+        l1 = min(L, l0 + chunk)
+        buf = _stage_buffer(dev, max(1, sum(halves[l0:l1])) * per_layer)
+        sk, sv, o = [], [], 0
+        for l in range(l0, l1):
+            for src, dst in ((ks[l], sk), (vs[l], sv)):
+                if src is None:
+                    dst.append(None)
+                    continue
+                st = buf[o * per_layer:(o + 1) * per_layer].view(b, h, n_kept, d)
+                o += 1
+                gather_rows(src, kept_idx, n_kept, kept_count, out=st, device=dev)
+                dst.append(st)
+        outs += compress_layers(sk, sv, key_levels=klv[l0:l1], value_levels=vlv[l0:l1], kept_count=kept_count,
+                                n_kept=n_kept, positions=pos, rope_base=rope_base, rope_scaling=rope_scaling,
+                                emit_codes=emit_codes, emit_scales_f32=emit_scales_f32, key_sharpen=key_sharpen,
+                                rope_rows=rope_rows or T, rotate=rotate,
+                                codes_out=None if codes_out is None else codes_out[l0:l1],
+                                _rows_known=rows_known)
     return outs
 
 

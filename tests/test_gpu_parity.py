@@ -309,6 +309,11 @@ def test_host_resident_inputs_match_device(orc):
     for a, b in ((ref.k_codes, got.k_codes), (ref.v_codes, got.v_codes), (ref.k_scales, got.k_scales),
                  (ref.v_scales, got.v_scales)):
         assert torch.equal(a, b)
+    direct = K.compress_layers([hk], [hv], key_levels=8, value_levels=4, kept_idx=kept, device=DEV,
+                               stage_host_rows=False)[0]
+    for a, b in ((ref.k_codes, direct.k_codes), (ref.v_codes, direct.v_codes), (ref.k_scales, direct.k_scales),
+                 (ref.v_scales, direct.v_scales)):
+        assert torch.equal(a, b)
     assert torch.equal(K.gather_rows(kd, kept, 111), K.gather_rows(hk, kept, 111, device=DEV))
     with pytest.raises(RuntimeError):
         K.compress_layers([k], [v], key_levels=8, value_levels=4, kept_idx=kept, device=DEV)  # not pinned
@@ -317,6 +322,44 @@ def test_host_resident_inputs_match_device(orc):
         N.call("nq_gather_rows", k.data_ptr(), 0, 2, 4, 128, *k.stride()[:3], kept.data_ptr(), None, 111,
                torch.empty((2, 4, 111, 128), dtype=torch.float16, device=DEV).data_ptr(), 4 * 111 * 128,
                111 * 128, 128, None)
+
+
+@pytest.mark.parametrize("explicit_positions", [False, True])
+def test_host_staged_compress_ragged_chunks(explicit_positions, monkeypatch):
+    """Staged host path (kept rows gathered into device memory, then compressed) against the
+    kernel reading the host rows itself and against device-resident layers: ragged kept
+    counts, a missing half, explicit positions and staging split into several chunks."""
+    cfg = syn.CacheConfig("t", 1, 2, 3, 400, 128)
+    layers = [syn.cpu_layer(cfg, l) for l in range(5)]
+    assert layers[0][0].dtype == torch.float16
+    rng = np.random.default_rng(5)
+    n_kept = 150
+    kept = torch.as_tensor(np.stack([np.sort(rng.choice(400, n_kept, replace=False)) for _ in range(2)]),
+                           dtype=torch.int32, device=DEV)
+    cnt = torch.tensor([150, 97], dtype=torch.int32, device=DEV)
+    pos = (kept + 1000) if explicit_positions else None
+    ks = [k for k, _ in layers]
+    vs = [v for _, v in layers]
+    vs[2] = None
+    hks = [k.pin_memory() for k in ks]
+    hvs = [None if v is None else v.pin_memory() for v in vs]
+    dks = [k.to(DEV) for k in ks]
+    dvs = [None if v is None else v.to(DEV) for v in vs]
+    kw = dict(key_levels=[4, 8, 16, 2, 4], value_levels=4, kept_idx=kept, kept_count=cnt, positions=pos)
+    ref = K.compress_layers(dks, dvs, **kw)
+    monkeypatch.setattr(K, "_STAGE_LIMIT", 2 * 2 * 2 * 3 * n_kept * 128 * 2)  # two layers per chunk
+    staged = K.compress_layers(hks, hvs, device=DEV, **kw)
+    direct = K.compress_layers(hks, hvs, device=DEV, stage_host_rows=False, **kw)
+    for got in (staged, direct):
+        for a, b in zip(ref, got):
+            for bi in range(2):
+                n = int(cnt[bi])
+                for x, y in ((a.k_codes, b.k_codes), (a.v_codes, b.v_codes), (a.k_scales, b.k_scales),
+                             (a.v_scales, b.v_scales)):
+                    if x is None:
+                        assert y is None
+                        continue
+                    assert torch.equal(x[bi, :, :n], y[bi, :, :n])
 
 
 def _attend_ref(q, ok, ov, count, scale):
