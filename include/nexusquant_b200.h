@@ -286,6 +286,40 @@ size_t nq_attend_compressed_workspace_size(int32_t batch, int32_t q_heads, int32
 nq_status_t nq_attend_compressed(const nq_attend_params_t *params, void *workspace, size_t workspace_bytes,
                                  nq_stream_t stream);
 
+/*
+ * Merge eviction, the value merging of NexusQuantEvict(merge_eviction=True)
+ * (nexusquant/pipeline.py:961-1048, called at :1186-1187 before hard eviction).  Four
+ * stream-ordered steps per batch element, all on device memory:
+ *
+ *   nq_merge_centroid_accumulate  centroid_sum[t, :] (+)= mean over heads of V_l[h, t, :] for
+ *                                 each given layer in order (accumulate = 0 starts the sum with
+ *                                 the first layer).  values: host array of n_layers device
+ *                                 pointers, each [heads, seq, head_dim] of one batch element with
+ *                                 strides (stride_h, stride_t, 1) in elements; 16-byte aligned.
+ *   nq_merge_centroid_normalize   unit_rows = (centroid_sum / n_layers) / max(||.||, 1e-12) per row
+ *                                 (pipeline.py:1013-1020); unit_rows may alias centroid_sum.
+ *   nq_merge_nearest              nearest[i] = argmax_j unit[evict_pos[i]] . unit[kept_pos[j]],
+ *                                 first j on ties (pipeline.py:1023-1024); head_dim a multiple of
+ *                                 32, at most 256.
+ *   nq_merge_apply                for each j with seg_start[j] < seg_start[j+1]:
+ *                                 V_l[h, kept_pos[j], :] += w * V_l[h, e, :] for e in
+ *                                 seg_evicted[seg_start[j] .. seg_start[j+1]) in that order,
+ *                                 w = fp32(imp[e] / (imp[s] + imp[e] + 1e-8)) in double, product
+ *                                 and sum rounded to fp32, stored once in the cache dtype
+ *                                 (pipeline.py:1026-1048).  In place; importance is fp32 [seq].
+ */
+nq_status_t nq_merge_centroid_accumulate(const void *const *values, int32_t n_layers, int32_t dtype, int32_t heads,
+                                         int32_t seq, int32_t head_dim, int64_t stride_h, int64_t stride_t,
+                                         int32_t accumulate, float *centroid_sum, nq_stream_t stream);
+nq_status_t nq_merge_centroid_normalize(const float *centroid_sum, int32_t seq, int32_t head_dim,
+                                        int32_t n_layers, float *unit_rows, nq_stream_t stream);
+nq_status_t nq_merge_nearest(const float *unit_rows, int32_t head_dim, const int32_t *evict_pos, int32_t n_evict,
+                             const int32_t *kept_pos, int32_t n_kept, int32_t *nearest, nq_stream_t stream);
+nq_status_t nq_merge_apply(const void *const *values, int32_t n_layers, int32_t dtype, int32_t heads, int32_t seq,
+                           int32_t head_dim, int64_t stride_h, int64_t stride_t, const float *importance,
+                           const int32_t *kept_pos, int32_t n_kept, const int32_t *seg_start,
+                           const int32_t *seg_evicted, nq_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

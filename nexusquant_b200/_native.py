@@ -98,6 +98,12 @@ _PROTOS = {
     "nq_delta_codes": (c_i32, [c_vp, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp]),
     "nq_attend_compressed_workspace_size": (c_size, [c_i32, c_i32, c_i32, c_i32]),
     "nq_attend_compressed": (c_i32, [ctypes.POINTER(AttendParams), c_vp, c_size, c_vp]),
+    "nq_merge_centroid_accumulate": (c_i32, [ctypes.POINTER(c_vp), c_i32, c_i32, c_i32, c_i32, c_i32, c_i64,
+                                             c_i64, c_i32, c_vp, c_vp]),
+    "nq_merge_centroid_normalize": (c_i32, [c_vp, c_i32, c_i32, c_i32, c_vp, c_vp]),
+    "nq_merge_nearest": (c_i32, [c_vp, c_i32, c_vp, c_i32, c_vp, c_i32, c_vp, c_vp]),
+    "nq_merge_apply": (c_i32, [ctypes.POINTER(c_vp), c_i32, c_i32, c_i32, c_i32, c_i32, c_i64, c_i64, c_vp, c_vp,
+                               c_i32, c_vp, c_vp, c_vp]),
 }
 
 EXPORTED = tuple(_PROTOS)

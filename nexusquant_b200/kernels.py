@@ -427,6 +427,72 @@ def gather_rows(x: torch.Tensor, kept_idx: Optional[torch.Tensor], n_kept: int,
     return out
 
 
+def merge_evicted_values(vs: Sequence[torch.Tensor], keep_mask: torch.Tensor, importance: torch.Tensor,
+                         nearest_out: Optional[List[torch.Tensor]] = None) -> None:
+    """Merge eviction, in place on ``vs`` (nexusquant/pipeline.py:961-1048): for every batch
+    element, each evicted token's values are added into the kept token whose value centroid
+    (mean over layers and heads) is most cosine-similar, weighted by
+    imp[e] / (imp[s] + imp[e] + 1e-8).  Layers whose sequence length differs from the mask's
+    are skipped, as the reference skips sliding-window layers.  ``nearest_out`` (optional list)
+    receives, per batch element, the chosen kept index of every evicted token (or None)."""
+    b, T = keep_mask.shape
+    layers = [v for v in vs if v.shape[2] == T]
+    _require_cuda(keep_mask, importance, *layers)
+    if nearest_out is not None:
+        nearest_out.clear()
+    if not layers:
+        if nearest_out is not None:
+            nearest_out.extend([None] * b)
+        return
+    ref = layers[0]
+    dev = ref.device
+    d = ref.shape[3]
+    for v in layers:
+        if v.shape[0] != b or v.shape[3] != d or v.dtype not in _DTYPES or v.stride(3) != 1:
+            raise ValueError("merge eviction needs [b, h, T, d] value layers with a common d and unit inner stride")
+    imp = importance.to(device=dev, dtype=torch.float32)
+    stream = _stream(dev)
+    # runs of consecutive layers sharing heads, dtype and strides go in one call, in layer order
+    runs = []
+    for v in layers:
+        key = (v.shape[1], v.dtype, v.stride(1), v.stride(2))
+        if runs and runs[-1][0] == key:
+            runs[-1][1].append(v)
+        else:
+            runs.append((key, [v]))
+    acc = torch.empty((T, d), dtype=torch.float32, device=dev)
+    for bi in range(b):
+        km = keep_mask[bi].to(dev)
+        evict = torch.nonzero(~km).flatten().to(torch.int32)
+        kept = torch.nonzero(km).flatten().to(torch.int32)
+        n_e, n_k = evict.numel(), kept.numel()
+        if n_e == 0 or n_k == 0:
+            if nearest_out is not None:
+                nearest_out.append(None)
+            continue
+        first = True
+        for (h, dt, sh, st), vl in runs:
+            ptrs = (ctypes.c_void_p * len(vl))(*[v[bi].data_ptr() for v in vl])
+            N.call("nq_merge_centroid_accumulate", ptrs, len(vl), _DTYPES[dt], h, T, d, sh, st, 0 if first else 1,
+                   acc.data_ptr(), stream)
+            first = False
+        N.call("nq_merge_centroid_normalize", acc.data_ptr(), T, d, len(layers), acc.data_ptr(), stream)
+        nearest = torch.empty(n_e, dtype=torch.int32, device=dev)
+        N.call("nq_merge_nearest", acc.data_ptr(), d, evict.data_ptr(), n_e, kept.data_ptr(), n_k,
+               nearest.data_ptr(), stream)
+        order = torch.argsort(nearest, stable=True)
+        seg_evicted = evict[order].contiguous()
+        seg_start = torch.zeros(n_k + 1, dtype=torch.int32, device=dev)
+        seg_start[1:] = torch.cumsum(torch.bincount(nearest, minlength=n_k), 0).to(torch.int32)
+        imp_b = imp[bi].contiguous()
+        for (h, dt, sh, st), vl in runs:
+            ptrs = (ctypes.c_void_p * len(vl))(*[v[bi].data_ptr() for v in vl])
+            N.call("nq_merge_apply", ptrs, len(vl), _DTYPES[dt], h, T, d, sh, st, imp_b.data_ptr(), kept.data_ptr(),
+                   n_k, seg_start.data_ptr(), seg_evicted.data_ptr(), stream)
+        if nearest_out is not None:
+            nearest_out.append(nearest)
+
+
 def delta_codes(codes: torch.Tensor, head_dim_padded: int, levels: int) -> torch.Tensor:
     """Temporal delta (nexusquant/core/temporal_codec.py:30-52) of packed codes [..., n, pb] -> int8 [..., n, d_p]."""
     _require_cuda(codes)

@@ -428,10 +428,13 @@ class NexusQuantEvict:
         skip = self._skip_layers(past_key_values, n_layers)
         if self.min_context_for_compression > 0 and seq < self.min_context_for_compression:
             return past_key_values, torch.ones(b, seq, device=device)
-        if self.merge_eviction:
-            raise NotImplementedError("merge_eviction is not part of the B200 compression path")
         levels = [self._resolve_layer_levels(l, n_layers) for l in range(n_layers)]
         ks, vs = zip(*[_get_layer_kv(past_key_values, l) for l in range(n_layers)])
+        if self.merge_eviction and not self.soft_eviction:
+            # value merging before hard eviction (pipeline.py:1185-1187), on copies of the
+            # full-length layers as the reference writes merged clones into the cache
+            vs = [v.clone() if v.shape[2] == seq else v for v in vs]
+            K.merge_evicted_values(vs, mask > 0, importance)
         if self.layout == "compressed":
             if self.soft_eviction:
                 raise NotImplementedError("soft_eviction has no compressed layout (all tokens stay visible)")

@@ -12,6 +12,7 @@ pipeline (jagmarques/nexusquant v0.5.0):
   key-key importance   nexusquant/pipeline.py:756-782 (_score_importance)
   real-attention score nexusquant/pipeline.py:826-836 applied to synthetic queries
   n_keep formula       nexusquant/pipeline.py:918-920 (IEEE double, as written)
+  merge eviction       nexusquant/pipeline.py:961-1048 (_apply_merge_eviction)
 """
 from __future__ import annotations
 
@@ -297,3 +298,67 @@ def boundary_groups(nrm_ref, nrm_mine=None, levels: int = 8, tol: float = 1e-6):
         near_gap = (gs[:, 1] - gs[:, 0]) < tol
         amb |= differs & (near_round.any(1) | near_gap)
     return amb.reshape(np.asarray(nrm_ref).shape[0], -1)
+
+
+# ----------------------------------------------------------------- merge eviction
+def merge_unit_centroids(vs_b):
+    """Unit-norm value centroids of one batch element (nexusquant/pipeline.py:996-1020):
+    mean over heads per layer, summed over the layers in order, divided by their count,
+    then x / max(||x||, 1e-12).  vs_b: list of [h, T, d] arrays (full-length layers only)."""
+    acc = None
+    for v in vs_b:
+        m = v.astype(np.float32).mean(axis=0, dtype=np.float32)
+        acc = m if acc is None else (acc + m).astype(np.float32)
+    c = (acc / np.float32(len(vs_b))).astype(np.float32)
+    n = np.sqrt((c.astype(np.float64) ** 2).sum(-1)).astype(np.float32)
+    return (c / np.maximum(n, np.float32(1e-12))[:, None]).astype(np.float32)
+
+
+def merge_similarity(unit, evict_pos, kept_pos):
+    """Cosine similarity [n_evict, n_kept] (pipeline.py:1016-1023), in float64 so that the
+    tests can tell a genuine argmax from a near tie."""
+    return unit[evict_pos].astype(np.float64) @ unit[kept_pos].astype(np.float64).T
+
+
+def merge_apply(vs_b, imp_b, evict_pos, kept_pos, nearest):
+    """The accumulation loop of pipeline.py:1026-1048 for one batch element, on float32 copies:
+    for each evicted position in ascending order, v[:, s] = fl32(v[:, s] + fl32(w32 * v[:, e]))
+    with w32 = float32(imp_e / (imp_s + imp_e + 1e-8)) evaluated in double (Python floats) --
+    torch casts the Python scalar to float32 before the multiply.  Returns new arrays in the
+    input dtype."""
+    out = []
+    for v in vs_b:
+        f = v.astype(np.float32)
+        for ei, e in enumerate(evict_pos):
+            s_ = kept_pos[nearest[ei]]
+            ie, is_ = float(imp_b[e]), float(imp_b[s_])
+            w = np.float32(ie / (is_ + ie + 1e-8))
+            f[:, s_, :] = (f[:, s_, :] + (f[:, e, :] * w).astype(np.float32)).astype(np.float32)
+        out.append(f.astype(v.dtype))
+    return out
+
+
+def merge_values(vs, keep_mask_, importance, nearest=None):
+    """Whole merge step over [b, h, T, d] layers (pipeline.py:977-1048).  Layers of another
+    length are returned unchanged.  nearest: optional per-batch argmax override (to replay a
+    device choice that differs from this one only on a near tie).  Returns (layers, nearest)."""
+    b, T = keep_mask_.shape
+    out = [np.array(v, copy=True) for v in vs]
+    full = [i for i, v in enumerate(vs) if v.shape[2] == T]
+    chosen = []
+    for bi in range(b):
+        km = keep_mask_[bi].astype(bool)
+        ev, kp = np.nonzero(~km)[0], np.nonzero(km)[0]
+        if ev.size == 0 or kp.size == 0 or not full:
+            chosen.append(None)
+            continue
+        if nearest is not None and nearest[bi] is not None:
+            nr = np.asarray(nearest[bi])
+        else:
+            unit = merge_unit_centroids([vs[i][bi] for i in full])
+            nr = merge_similarity(unit, ev, kp).argmax(axis=1)
+        chosen.append(nr)
+        merged = merge_apply([out[i][bi] for i in full], importance[bi], ev, kp, nr)
+        for i, m in zip(full, merged):
+            out[i][bi] = m
+    return out, chosen

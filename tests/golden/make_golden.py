@@ -3,6 +3,7 @@
 Run in a container that has the reference checked out (read-only is fine):
 
     PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py --ref /path/to/nexusquant
+    (--part merge regenerates only merge.npz)
 
 The reference is jagmarques/nexusquant v0.5.0.  Every fixture is produced by the
 reference's own functions on seeded inputs (nexusquant_b200.synthetic or small
@@ -95,11 +96,49 @@ def diff_record(prefix, codes_ref, nrm_ref, x_rows, d_p, levels, cos=None, sin=N
     return out
 
 
+def make_merge(P) -> dict:
+    """Merge eviction (pipeline.py:961-1048) run by the reference itself: the merged values of
+    _apply_merge_eviction on a cache with one shorter (skipped) layer, and the fake-quant output
+    of a full compress(merge_eviction=True).  Written to merge.npz."""
+    fx = {}
+    cfg = syn.CacheConfig("merge", 4, 2, 2, 96, 128)
+    ks_, vs_ = zip(*[syn.cpu_layer(cfg, l, seq=(64 if l == 2 else None)) for l in range(4)])
+    ev = P.NexusQuantEvict(bits=2, eviction_rate=0.6, sliding_window=16, merge_eviction=True)
+    imp = ev._score_importance(ks_[0].float())
+    mask = ev._build_keep_mask(imp, 96, eviction_rate=0.6)
+    cache = FakeCache([k.clone() for k in ks_], [v.clone() for v in vs_])
+    ev._apply_merge_eviction(cache, mask, imp, 4)
+    fx["merge_importance"] = imp.numpy()
+    fx["merge_mask"] = mask.numpy()
+    fx["merge_in_sha"] = np.frombuffer(sha(torch.cat([t.reshape(-1) for t in ks_ + vs_])).encode(), np.uint8)
+    for l in range(4):
+        fx[f"merge_v{l}"] = cache.value_cache[l].numpy()
+    # full pipeline on the three full-length layers, boundary layers 0 and 2 kept at fp16
+    ev = P.NexusQuantEvict(bits=2, eviction_rate=0.6, sliding_window=16, protect_boundary=1, merge_eviction=True)
+    idx = [0, 1, 3]
+    cache = FakeCache([ks_[l].clone() for l in idx], [vs_[l].clone() for l in idx])
+    _, pm = ev.compress(cache)
+    fx["merge_pipe_mask"] = pm.numpy()
+    for i in range(3):
+        fx[f"merge_pipe_k{i}"] = cache.key_cache[i].numpy()
+        fx[f"merge_pipe_v{i}"] = cache.value_cache[i].numpy()
+    return fx
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("NQ_REFERENCE", "/root/reference"))
+    ap.add_argument("--part", choices=["all", "merge"], default="all",
+                    help="merge: write only merge.npz (merge eviction fixtures)")
     args = ap.parse_args()
     sys.path.insert(0, args.ref)
+    if args.part == "merge":
+        from nexusquant import pipeline as P
+        torch.set_num_threads(8)
+        out = os.path.join(HERE, "merge.npz")
+        np.savez_compressed(out, **make_merge(P))
+        print("wrote", out, os.path.getsize(out), "bytes")
+        return
     from nexusquant.core.hadamard import hadamard_matrix
     from nexusquant.core.e8_lattice import E8Lattice
     from nexusquant.core import rope_utils
@@ -330,6 +369,9 @@ def main():
 
     out = os.path.join(HERE, "golden.npz")
     np.savez_compressed(out, **fx)
+    print("wrote", out, os.path.getsize(out), "bytes")
+    out = os.path.join(HERE, "merge.npz")
+    np.savez_compressed(out, **make_merge(P))
     print("wrote", out, os.path.getsize(out), "bytes")
 
 
