@@ -320,6 +320,23 @@ nq_status_t nq_merge_apply(const void *const *values, int32_t n_layers, int32_t 
                            const int32_t *kept_pos, int32_t n_kept, const int32_t *seg_start,
                            const int32_t *seg_evicted, nq_stream_t stream);
 
+/*
+ * Byte layouts of the paged interface (nexusquant/integrations/vllm_backend.py):
+ *   nq_unpack_codes    packed lattice codes [rows, nq_packed_bytes(d_p, levels)] -> int8
+ *                      [rows, d_p] with code = 2 x lattice point, the layout of
+ *                      CompressedPage.key_codes / value_codes (vllm_backend.py:73-101).
+ *                      codes must be 8-byte aligned.
+ *   nq_pack_nibbles    NexusQuantKVCompressor.pack_codes_nibble (vllm_backend.py:476-513):
+ *                      int8 [rows, d] -> uint8 [rows, (d + 1) / 2], byte k = clamp(c[2k] + 8)
+ *                      | clamp(c[2k+1] + 8) << 4 (clamp to [0, 15]; an odd d pads a 0 nibble).
+ *   nq_unpack_nibbles  unpack_codes_nibble (vllm_backend.py:515-540): the inverse, nibble - 8.
+ * Replace the reference's torch byte manipulation on the page path; one pass each.
+ */
+nq_status_t nq_unpack_codes(const uint8_t *packed, int64_t rows, int32_t head_dim_padded, int32_t levels,
+                            int8_t *codes, nq_stream_t stream);
+nq_status_t nq_pack_nibbles(const int8_t *codes, int64_t rows, int32_t d, uint8_t *packed, nq_stream_t stream);
+nq_status_t nq_unpack_nibbles(const uint8_t *packed, int64_t rows, int32_t d, int8_t *codes, nq_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -13,6 +13,7 @@ pipeline (jagmarques/nexusquant v0.5.0):
   real-attention score nexusquant/pipeline.py:826-836 applied to synthetic queries
   n_keep formula       nexusquant/pipeline.py:918-920 (IEEE double, as written)
   merge eviction       nexusquant/pipeline.py:961-1048 (_apply_merge_eviction)
+  nibble packing       nexusquant/integrations/vllm_backend.py:476-540
 """
 from __future__ import annotations
 
@@ -362,3 +363,20 @@ def merge_values(vs, keep_mask_, importance, nearest=None):
         for i, m in zip(full, merged):
             out[i][bi] = m
     return out, chosen
+
+
+# ------------------------------------------------------------------- page nibbles
+def pack_codes_nibble(codes):
+    """vllm_backend.py:476-513: c = clamp(code + 8, 0, 15); an odd last dim is padded with a
+    0 nibble; byte = c_even | c_odd << 4."""
+    c = np.clip(np.asarray(codes).astype(np.int32) + 8, 0, 15)
+    if c.shape[-1] % 2:
+        c = np.concatenate([c, np.zeros(c.shape[:-1] + (1,), np.int32)], axis=-1)
+    return ((c[..., 0::2] & 0xF) | ((c[..., 1::2] & 0xF) << 4)).astype(np.uint8)
+
+
+def unpack_codes_nibble(packed, original_d: int):
+    """vllm_backend.py:515-540: low nibble then high nibble, minus 8, first original_d."""
+    p = np.asarray(packed).astype(np.int32)
+    both = np.stack([p & 0xF, (p >> 4) & 0xF], axis=-1).reshape(p.shape[:-1] + (-1,))
+    return (both[..., :original_d] - 8).astype(np.int8)
