@@ -383,6 +383,81 @@ def run_reference(args, cfg, rank, world):
     print(json.dumps(line), flush=True)
 
 
+# --------------------------------------------------------------- kernel modes
+def run_kernel(args, cfg, dev):
+    """--kernel attend|merge: one JSON line timing a compressed-cache kernel outside the
+    headline step, on the bench's synthetic layers of the chosen config (1 GPU, CUDA events).
+
+    attend: decode attention over one compressed layer (kernels.attend_compressed) with 8 query
+            heads per KV head, against dequantize + torch attention of the same codes.
+    merge : merge eviction (kernels.merge_evicted_values) over --merge-layers layers; each
+            timed iteration starts from the original values (restored outside the timing)."""
+    T, h, d = cfg.seq, cfg.heads, cfg.head_dim
+    kl, vl = 2 ** cfg.key_bits, 2 ** cfg.value_bits
+    k0, _ = syn.device_layer(cfg, 0, dev)
+    imp = K.score_keykey(k0, 32)
+    nk = n_keep_for(T, cfg.sliding_window, cfg.eviction_rate)
+    idx, cnt = K.select_keep(imp, cfg.sliding_window, nk)
+    cap = int(cnt.max())
+    line = {"impl": "ours", "n_gpus": 1, "data": "synthetic", "config": {"workload": cfg.name, "seq": T, "heads": h,
+                                                                          "head_dim": d, "kept_tokens": cap}}
+    if args.kernel == "attend":
+        k, v = syn.device_layer(cfg, 3, dev)
+        kidx = idx[:, :cap].contiguous()
+        lc = K.compress_layers([k], [v], key_levels=kl, value_levels=vl, kept_idx=kidx, kept_count=cnt, n_kept=cap,
+                               rope_base=cfg.rope_base)[0]
+        del k, v
+        hq = 8 * h
+        q = (torch.randn(cfg.batch, hq, d, device=dev, generator=torch.Generator(device=dev).manual_seed(0)) * 0.3).half()
+
+        def fused():
+            return K.attend_compressed(q, lc, kidx, count=cnt, rope_base=cfg.rope_base, rope_rows=T)
+
+        def unfused():
+            ok, ov = K.decompress_layers([lc], kidx, head_dim=d, count=cnt, rope_base=cfg.rope_base)
+            kk = ok[0][0].float().repeat_interleave(8, 0)
+            vv = ov[0][0].float().repeat_interleave(8, 0)
+            w = torch.softmax(torch.einsum("hd,hnd->hn", q[0].float(), kk) * d ** -0.5, -1)
+            return torch.einsum("hn,hnd->hd", w, vv).half()[None]
+
+        a, b = fused().float(), unfused().float()
+        rel = float((a - b).norm() / b.norm())
+        fms = timed(fused, args.steps, args.warmup, 1) / args.steps
+        ums = timed(unfused, args.steps, args.warmup, 1) / args.steps
+        nbytes = sum(t.numel() * t.element_size() for t in (lc.k_codes, lc.v_codes, lc.k_scales, lc.v_scales))
+        line.update({"metric": "decode attention over one compressed layer", "value": round(fms * 1e3, 2),
+                     "unit": "us", "higher_is_better": False, "q_heads": hq,
+                     "compressed_bytes": nbytes, "gbs_of_compressed_bytes": round(nbytes / fms / 1e6, 1),
+                     "dequant_then_torch_us": round(ums * 1e3, 2), "rel_l2_vs_dequant_then_torch": rel})
+    else:
+        L = args.merge_layers
+        vs = [syn.device_layer(cfg, l, dev)[1] for l in range(L)]
+        backup = [v.clone() for v in vs]
+        mask = torch.zeros(cfg.batch, T + 1, dtype=torch.bool, device=dev)
+        valid = torch.arange(idx.shape[1], device=dev)[None] < cnt[:, None]
+        mask.scatter_(1, torch.where(valid, idx.long(), torch.full_like(idx.long(), T)), True)
+        mask = mask[:, :T].contiguous()
+        times = []
+        for it in range(args.warmup + 5):
+            for v, bk in zip(vs, backup):
+                v.copy_(bk)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            K.merge_evicted_values(vs, mask, imp)
+            e1.record()
+            torch.cuda.synchronize()
+            if it >= args.warmup:
+                times.append(e0.elapsed_time(e1))
+        ms = sorted(times)[len(times) // 2]
+        n_e = int((~mask).sum())
+        fma = n_e * cap * d * cfg.batch
+        line.update({"metric": "merge eviction over layers", "value": round(ms, 3), "unit": "ms",
+                     "higher_is_better": False, "layers": L, "evicted_tokens": n_e,
+                     "similarity_fma": fma, "similarity_tflops_if_all_time": round(2 * fma / ms / 1e9, 1)})
+    print(json.dumps(line), flush=True)
+
+
 # ------------------------------------------------------------------------ main
 def main():
     ap = argparse.ArgumentParser()
@@ -395,6 +470,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--profile", action="store_true", help="a few steps only (for ncu launch lists)")
+    ap.add_argument("--kernel", choices=["attend", "merge"], default=None,
+                    help="time one compressed-cache kernel instead of the headline step (1 GPU)")
+    ap.add_argument("--merge-layers", type=int, default=8)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     # Native libraries (NCCL's version banner, for one) print to fd 1; the driver reads the one
@@ -413,6 +491,10 @@ def main():
         return
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    if args.kernel is not None:
+        if rank == 0:
+            run_kernel(args, cfg, dev)
+        return
     group = None
     if world > 1:
         dist.init_process_group("nccl", device_id=dev)

@@ -151,14 +151,14 @@ nq_status_t nq_decompress_layers(const nq_decompress_params_t* p, nq_stream_t st
       if (q && !aligned16(q)) return NQ_ERR_ALIGNMENT;
     any_key |= (L.k_codes != nullptr);
   }
-  if (any_key && (!p->positions || !p->rope_cos || !p->rope_sin)) return NQ_ERR_INVALID_ARG;
+  if (any_key && (!p->positions || !p->rope_cos || !p->rope_sin || p->rope_rows <= 0)) return NQ_ERR_INVALID_ARG;
   nq::DecompressArgs a;
   std::memset(&a, 0, sizeof(a));
   a.batch = p->batch; a.heads = p->heads; a.n_tokens = p->n_tokens;
   a.head_dim = p->head_dim; a.head_dim_padded = p->head_dim_padded;
   a.head_group = head_group_for(p->heads);
   a.count = p->count; a.positions = p->positions;
-  a.rope_cos = p->rope_cos; a.rope_sin = p->rope_sin;
+  a.rope_cos = p->rope_cos; a.rope_sin = p->rope_sin; a.rope_rows = p->rope_rows;
   a.out_stride_b = p->out_stride_b; a.out_stride_h = p->out_stride_h; a.out_stride_t = p->out_stride_t;
   a.key_sharpen = p->key_sharpen == 0.0f ? 1.0f : p->key_sharpen;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -348,7 +348,7 @@ nq_status_t nq_attend_compressed(const nq_attend_params_t* p, void* workspace, s
   a.q = reinterpret_cast<const __half*>(p->q);
   a.q_stride_b = p->q_stride_b; a.q_stride_h = p->q_stride_h;
   a.k_codes = p->k_codes; a.v_codes = p->v_codes; a.k_scales = p->k_scales; a.v_scales = p->v_scales;
-  a.positions = p->positions; a.rope_cos = p->rope_cos; a.rope_sin = p->rope_sin;
+  a.positions = p->positions; a.rope_cos = p->rope_cos; a.rope_sin = p->rope_sin; a.rope_rows = p->rope_rows;
   a.key_sharpen = p->key_sharpen == 0.0f ? 1.0f : p->key_sharpen;
   a.scale = p->scale == 0.0f ? 1.0f / sqrtf((float)p->head_dim) : p->scale;
   a.out = reinterpret_cast<__half*>(p->out);

@@ -161,7 +161,7 @@ __global__ void __launch_bounds__(kAtTok) attend_partial(const AttendArgs a) {
 #pragma unroll
       for (int q = 0; q < 64; ++q) R[q] = __hfma2(__high2half2(R[q]), pm, __low2half2(R[q]));
       const float coef = __fmul_rn(__half2float(__ushort_as_half(a.k_scales[row0 + t])), coef_h);
-      const int pos = a.positions[(int64_t)b * a.n_tokens + t];
+      const int pos = min(max(a.positions[(int64_t)b * a.n_tokens + t], 0), a.rope_rows - 1);
       const float* cs = a.rope_cos + (int64_t)pos * (kAtD / 2);
       const float* sn = a.rope_sin + (int64_t)pos * (kAtD / 2);
 #pragma unroll

@@ -335,7 +335,9 @@ __device__ __forceinline__ void issue_tile(const CompressArgs& a, const Tile& t,
   if (key) {
     // the warp's tokens: vectors wv0 .. wv0+15 -> tokens wv0/HG .. (wv0+15)/HG
     constexpr int HALF = (D / 2) * 4 / 16;  // chunks of one cos (or sin) row
-    const int pos = vj ? (a.positions ? a.positions[(int64_t)t.b * a.n_kept + j] : row) : -1;
+    // clamped into the table: a position past it must not read outside the RoPE rows
+    const int pos = vj ? min(max(a.positions ? a.positions[(int64_t)t.b * a.n_kept + j] : row, 0), a.rope_rows - 1)
+                       : -1;
     const int tw0 = wv0 / HG, ntw = (WV + HG - 1) / HG;  // tokens of this warp
     const int n_chunks = ntw * 2 * HALF;
     for (int c0 = 0; c0 < n_chunks; c0 += 32) {  // uniform trip count: the shuffle needs every lane
@@ -555,11 +557,12 @@ __device__ __forceinline__ void compress_tile(const CompressArgs& a, const Tile&
         }
       if (valid && h == 0) {
         const int src_row = a.kept_idx ? a.kept_idx[(int64_t)t.b * a.n_kept + j] : j;
-        const int pos = a.positions ? a.positions[(int64_t)t.b * a.n_kept + j] : src_row;
+        const int pos = min(max(a.positions ? a.positions[(int64_t)t.b * a.n_kept + j] : src_row, 0), a.rope_rows - 1);
         const int orow = a.out_row_mode == 1 ? j : src_row;
         int opos = pos;
         if (a.out_positions) opos = a.out_positions[(int64_t)t.b * a.n_kept + j];
         else if (a.out_row_mode == 1) opos = j;
+        opos = min(max(opos, 0), a.rope_rows - 1);
         __half* o = reinterpret_cast<__half*>(out) + (int64_t)t.b * a.out_stride_b +
                     (int64_t)head * a.out_stride_h + (int64_t)orow * a.out_stride_t;
         recon_store<D, DP>(x, sc, KEY, a.rope_cos + (int64_t)opos * (D / 2), a.rope_sin + (int64_t)opos * (D / 2),

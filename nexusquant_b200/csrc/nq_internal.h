@@ -61,6 +61,7 @@ struct DecompressArgs {
   const int32_t* positions;
   const float* rope_cos;
   const float* rope_sin;
+  int32_t rope_rows;  // positions are clamped to [0, rope_rows - 1] before indexing the tables
   int64_t out_stride_b, out_stride_h, out_stride_t;
   float key_sharpen;
   DLayerIO layers[kMaxLayersPerLaunch];
@@ -118,6 +119,7 @@ struct AttendArgs {
   const int32_t* positions;
   const float* rope_cos;
   const float* rope_sin;
+  int32_t rope_rows;  // positions are clamped to [0, rope_rows - 1] before indexing the tables
   float key_sharpen, scale;
   float* ws_m;    // [b, hq, splits]
   float* ws_l;    // [b, hq, splits]

@@ -214,7 +214,7 @@ __device__ __forceinline__ void decompress_vector(const DecompressArgs& args, co
     // butterfly runs (they are consecutive lanes of one warp)
     trow = reinterpret_cast<float*>(rope_smem + (threadIdx.x / HG) * RopeSmem<D>::kRow);
     if (valid) {
-      const int pos = args.positions[(int64_t)b * args.n_tokens + j];
+      const int pos = min(max(args.positions[(int64_t)b * args.n_tokens + j], 0), args.rope_rows - 1);
       const int hl = threadIdx.x % HG;
       for (int c = hl; c < RopeSmem<D>::kChunks; c += HG) {
         const int half = c / (RopeSmem<D>::kChunks / 2), k = c % (RopeSmem<D>::kChunks / 2);

@@ -544,13 +544,16 @@ def e8_quantize_perhead(x: torch.Tensor, levels: int = 4) -> torch.Tensor:
 def attend_compressed(q: torch.Tensor, codes: LayerCodes, positions: torch.Tensor, *,
                       count: Optional[torch.Tensor] = None, rope_base: float = 10000.0,
                       rope_scaling: Optional[dict] = None, key_sharpen: float = 1.0,
-                      scale: Optional[float] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                      scale: Optional[float] = None, out: Optional[torch.Tensor] = None,
+                      rope_rows: Optional[int] = None) -> torch.Tensor:
     """Decode attention over one compressed layer (NexusQuantPagedAttention.forward,
     vllm_backend.py:692-765) without materialising fp16 K/V.
 
     q         : fp16 [b, hq, 128], one query token per sequence (RoPE already applied).
     codes     : LayerCodes of the layer ([b, h, n, pb] codes, [b, h, n] fp16 scales); hq / h in {1,2,4,8}.
     positions : int32 [b, n] RoPE positions of the stored keys.
+    rope_rows : RoPE table rows to use when every position is known to be below it; None reads
+                positions.max() (a host synchronisation) to size the table.
     Returns fp16 [b, hq, 128] = softmax(q K^T * scale) V with K, V as decompress_layers gives them."""
     _require_cuda(q, positions, count)
     b, hq, d = q.shape
@@ -562,7 +565,10 @@ def attend_compressed(q: torch.Tensor, codes: LayerCodes, positions: torch.Tenso
     positions = positions.to(device=dev, dtype=torch.int32).contiguous()
     if count is not None:
         count = count.to(device=dev, dtype=torch.int32).contiguous()
-    rows = int(positions.max().item()) + 1 if positions.numel() else 1
+    if rope_rows is not None:
+        rows = int(rope_rows)
+    else:
+        rows = int(positions.max().item()) + 1 if positions.numel() else 1
     cos, sin = TABLES.get(dev, d, rope_base, rows, rope_scaling)
     if out is None:
         out = torch.empty((b, hq, d), dtype=torch.float16, device=dev)

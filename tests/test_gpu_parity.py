@@ -395,3 +395,23 @@ def test_attend_compressed_vs_decompress_then_attention(orc, lk, lv, g, sharpen)
     assert rel_l2(got.cpu().numpy(), ref.cpu().numpy()) < REL_L2_TOL
     again = K.attend_compressed(q, lc, pos, count=count, key_sharpen=sharpen)
     assert torch.equal(got, again)  # deterministic
+
+
+def test_positions_past_the_rope_table_are_clamped():
+    """A stored position at or past the RoPE table (a caller's rope_rows too small) reads the
+    table's last row instead of memory past it: the output equals that of the clamped positions."""
+    from nexusquant_b200.rope import TABLES
+    cfg = syn.CacheConfig("t", 1, 1, 2, 64, 128)
+    k, v = syn.cpu_layer(cfg, 2)
+    base = 12345.0  # a table of its own, sized by this test
+    pos = torch.arange(64, dtype=torch.int32, device=DEV)[None]
+    lc = K.compress_layers([k.to(DEV)], [v.to(DEV)], key_levels=4, value_levels=4, positions=pos,
+                           rope_base=base, rope_rows=64)[0]
+    rows = TABLES.get(torch.device(DEV), 128, base, 16)[0].shape[0]
+    far = pos.clone()
+    far[0, 40:] += rows + 1000
+    q = torch.randn(1, 4, 128, device=DEV).half()
+    got = K.attend_compressed(q, lc, far, rope_base=base, rope_rows=rows)
+    want = K.attend_compressed(q, lc, far.clamp(max=rows - 1), rope_base=base, rope_rows=rows)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
