@@ -127,10 +127,13 @@ def make_merge(P) -> dict:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("NQ_REFERENCE", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("NQ_REFERENCE"),
+                    help="checkout of the reference (or set NQ_REFERENCE)")
     ap.add_argument("--part", choices=["all", "merge"], default="all",
                     help="merge: write only merge.npz (merge eviction fixtures)")
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("--ref (or NQ_REFERENCE) must name the reference checkout")
     sys.path.insert(0, args.ref)
     if args.part == "merge":
         from nexusquant import pipeline as P
