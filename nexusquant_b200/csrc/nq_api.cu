@@ -105,20 +105,19 @@ nq_status_t nq_compress_layers(const nq_compress_params_t* p, nq_stream_t stream
   a.rotate = p->rotate;
   a.error_flag = p->error_flag;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // one launch per (key format, value format) group of layers, at most kMaxLayersPerLaunch each
-  auto fmt = [](int levels) { return levels <= 4 ? 0 : (levels == 8 ? 1 : 2); };
+  // one launch per (key level count, value level count) group of layers (the kernels are
+  // specialised on the level count), at most kMaxLayersPerLaunch layers each
+  auto group_key = [&](int l) {
+    const nq_layer_io_t& L = p->layers[l];
+    return (L.k ? L.key_levels : 0) * 32 + (L.v ? L.value_levels : 0);
+  };
   std::vector<int> order(p->n_layers);
   for (int l = 0; l < p->n_layers; ++l) order[l] = l;
-  std::stable_sort(order.begin(), order.end(), [&](int x, int y) {
-    return fmt(p->layers[x].key_levels) * 3 + fmt(p->layers[x].value_levels) <
-           fmt(p->layers[y].key_levels) * 3 + fmt(p->layers[y].value_levels);
-  });
+  std::stable_sort(order.begin(), order.end(), [&](int x, int y) { return group_key(x) < group_key(y); });
   for (int l0 = 0; l0 < p->n_layers;) {
-    const int key0 = fmt(p->layers[order[l0]].key_levels) * 3 + fmt(p->layers[order[l0]].value_levels);
+    const int key0 = group_key(order[l0]);
     int n = 0;
-    while (l0 + n < p->n_layers && n < kMaxLayersPerLaunch &&
-           fmt(p->layers[order[l0 + n]].key_levels) * 3 + fmt(p->layers[order[l0 + n]].value_levels) == key0)
-      ++n;
+    while (l0 + n < p->n_layers && n < kMaxLayersPerLaunch && group_key(order[l0 + n]) == key0) ++n;
     for (int i = 0; i < n; ++i) {
       const nq_layer_io_t& L = p->layers[order[l0 + i]];
       nq::LayerIO& d = a.layers[i];
@@ -327,13 +326,14 @@ nq_status_t nq_attend_compressed(const nq_attend_params_t* p, void* workspace, s
   for (const void* q : al)
     if (!aligned16(q)) return NQ_ERR_ALIGNMENT;
   if (p->n_tokens == 0) {
-    // nothing to attend: zero outputs
-    for (int b = 0; b < p->batch; ++b)
-      for (int h = 0; h < p->q_heads; ++h) {
-        const cudaError_t e = cudaMemsetAsync(p->out + b * p->out_stride_b + h * p->out_stride_h, 0, 256,
-                                              static_cast<cudaStream_t>(stream));
-        if (e != cudaSuccess) return NQ_ERR_CUDA;
-      }
+    // nothing to attend: zero the [q_heads, 128] fp16 rows of each batch element (one strided
+    // memset per batch element)
+    if (p->out_stride_h < 128) return NQ_ERR_INVALID_ARG;
+    for (int b = 0; b < p->batch; ++b) {
+      const cudaError_t e = cudaMemset2DAsync(p->out + b * p->out_stride_b, (size_t)p->out_stride_h * 2, 0, 256,
+                                              (size_t)p->q_heads, static_cast<cudaStream_t>(stream));
+      if (e != cudaSuccess) return NQ_ERR_CUDA;
+    }
     return NQ_OK;
   }
   const int splits = nq::attend_splits(p->batch, p->heads, p->n_tokens);

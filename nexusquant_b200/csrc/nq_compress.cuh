@@ -82,9 +82,9 @@ __device__ __forceinline__ uint32_t umin(uint32_t a, uint32_t b) { return a < b 
 //  * clamping to [-L, L]: with L a power of two, sc = amax * 2/L is exact and |x| <= L/2,
 //    so a field leaves the range only as B at x = +L/2 (L >= 4, f = L + 9 + BIAS - 8),
 //    B at x = -L/2 (L = 2, f = 5), or the A step at a = +L/2 -- each is patched directly.
-template <int FMT>
+template <int FMT, int LEV>
 __device__ __forceinline__ void e8_group(const float (&e)[8], const uint32_t (&sa)[8], const uint32_t (&sb)[8],
-                                         int levels, uint32_t (&w)[GF<FMT>::kWords]) {
+                                         uint32_t (&w)[GF<FMT>::kWords]) {
   using F = GF<FMT>;
   constexpr int NW = F::kWords;
   const float gsum = __fadd_rn(__fadd_rn(__fadd_rn(fabsf(e[0]), fabsf(e[1])), __fadd_rn(fabsf(e[2]), fabsf(e[3]))),
@@ -98,6 +98,10 @@ __device__ __forceinline__ void e8_group(const float (&e)[8], const uint32_t (&s
   const uint32_t km = in_hi ? kh : kl;
   const uint32_t gbits = km >> 2;
   const int idx = (in_hi ? 4 : 0) + (int)(km & 3u);
+  // Sign bits of e (bit 7 - i for coordinate i), for the direction of the A step.
+  uint32_t neg = 0u;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) neg = __funnelshift_l(__float_as_uint(e[i]), neg, 1);
 
   uint32_t wa[NW], wb[NW];
 #pragma unroll
@@ -113,26 +117,27 @@ __device__ __forceinline__ void e8_group(const float (&e)[8], const uint32_t (&s
   const float lhs = par ? __fadd_rn(gsum, __fmaf_rn(-2.0f, __uint_as_float(gbits), 1.0f)) : gsum;
   const bool use_b = lhs > 2.0f;
 
-  // A step at coordinate idx
+  // A step at coordinate idx: one step toward x, up when e_idx >= 0 (e8_lattice.py:42-43;
+  // e = -0 only for x = -0, whose gap is 0 and which steps up)
   const int sh = F::kWidth * (FMT == 0 ? idx : (idx & 3));
   const uint32_t wa_i = (NW == 1 || idx < 4) ? wa[0] : wa[NW - 1];
-  const uint32_t wb_i = (NW == 1 || idx < 4) ? wb[0] : wb[NW - 1];
-  const int fa = (int)((wa_i >> sh) & F::kMask), fb = (int)((wb_i >> sh) & F::kMask);
-  const int d = gbits == 0u ? 2 : 2 * (fb - fa);
-  const bool step = par && !use_b && !(d > 0 && fa == F::kBias + levels);
-  const uint32_t delta = step ? ((uint32_t)d << sh) : 0u;
+  const uint32_t fa = (wa_i >> sh) & F::kMask;
+  const bool up = gbits == 0u || ((neg >> (7 - idx)) & 1u) == 0u;
+  // a = +L/2 cannot step up: the reference's clamp (e8_lattice.py:120) takes it back
+  const bool step = par && !use_b && !(up && fa == (uint32_t)(F::kBias + LEV));
+  const uint32_t delta = step ? ((up ? 2u : 0xfffffffeu) << sh) : 0u;
 
-  // B clamps
+  // B clamps (compile-time level count)
 #pragma unroll
   for (int k = 0; k < NW; ++k) {
     const uint32_t x = wb[k];
     if constexpr (FMT == 0) {
-      if (levels == 4) wb[k] = x - (x & (x >> 2) & (x >> 3) & F::kBit0);   // 13 -> 12
-      else wb[k] = x + (x & (x >> 2) & ~(x >> 1) & F::kBit0);            // L = 2: 5 -> 6
+      if constexpr (LEV == 4) wb[k] = x - (x & (x >> 2) & (x >> 3) & F::kBit0);  // 13 -> 12
+      else wb[k] = x + (x & (x >> 2) & ~(x >> 1) & F::kBit0);                     // L = 2: 5 -> 6
     } else if constexpr (FMT == 1) {
-      wb[k] = x - (x & (x >> 4) & F::kBit0);                              // 17 -> 16
+      wb[k] = x - (x & (x >> 4) & F::kBit0);                                      // 17 -> 16
     } else {
-      wb[k] = x - (x & (x >> 4) & (x >> 5) & F::kBit0);                   // 49 -> 48
+      wb[k] = x - (x & (x >> 4) & (x >> 5) & F::kBit0);                           // 49 -> 48
     }
   }
 #pragma unroll
@@ -258,22 +263,46 @@ struct Tile {
   int layer, kv, b, hg, tt;
 };
 
-// Decoded once per tile and iteration (32-bit: the host keeps the tile count below 2^31).
-__device__ __forceinline__ Tile decode_tile(const CompressArgs& a, int n_layers, int t) {
-  const int TOK = kCompressVecs / a.head_group;
-  const int t_tiles = (a.n_kept + TOK - 1) / TOK;
-  const int h_groups = (a.heads + a.head_group - 1) / a.head_group;
+// Tile-list geometry of one launch half, fixed per launch.
+struct TileGeom {
+  int tt_n;  // token tiles per (layer, batch, head group)
+  int hg_n;  // head groups
+};
+
+__device__ __forceinline__ TileGeom tile_geom(const CompressArgs& a) {
+  const int TOK = kCompressVecs >> a.hg_shift;
+  return TileGeom{(a.n_kept + TOK - 1) / TOK, (a.heads + a.head_group - 1) >> a.hg_shift};
+}
+
+// Decoded once per CTA (32-bit: the host keeps the tile count below 2^31).
+__device__ __forceinline__ Tile decode_tile(const CompressArgs& a, const TileGeom& g, int n_layers, int t) {
   Tile r;
-  int q = t / t_tiles;
-  r.tt = t - q * t_tiles;
-  t = q; q = t / h_groups;
-  r.hg = t - q * h_groups;
+  int q = t / g.tt_n;
+  r.tt = t - q * g.tt_n;
+  t = q; q = t / g.hg_n;
+  r.hg = t - q * g.hg_n;
   t = q; q = t / a.batch;
   r.b = t - q * a.batch;
   t = q; q = t / n_layers;
   r.layer = t - q * n_layers;
   r.kv = q;  // K tiles first, then V tiles
   return r;
+}
+
+// Advance a decoded tile by `step` tiles without dividing (the carry loop runs about
+// step / tt_n + 1 times; the layer index may run past the end, which the caller bounds).
+__device__ __forceinline__ void advance_tile(Tile& r, const CompressArgs& a, const TileGeom& g, int step) {
+  r.tt += step;
+  while (r.tt >= g.tt_n) {
+    r.tt -= g.tt_n;
+    if (++r.hg == g.hg_n) {
+      r.hg = 0;
+      if (++r.b == a.batch) {
+        r.b = 0;
+        ++r.layer;
+      }
+    }
+  }
 }
 
 template <typename TIn, int D>
@@ -309,12 +338,12 @@ __device__ __forceinline__ void issue_tile(const CompressArgs& a, const Tile& t,
   const bool key = t.kv == 0;
   const TIn* src = static_cast<const TIn*>(key ? L.k : L.v);
   if (src == nullptr) return;
-  const int HG = a.head_group, TOK = kCompressVecs / HG;
+  const int HG = a.head_group, TOK = kCompressVecs >> a.hg_shift;
   const int count = a.kept_count ? min(a.kept_count[t.b], a.n_kept) : a.n_kept;
   const int lane = threadIdx.x & 31, wv0 = (threadIdx.x >> 5) * WV;  // the warp's first vector
   // this lane's vector (lanes 2v, 2v+1 own vector v): its row address and RoPE position
   const int v = threadIdx.x >> 1;
-  const int tok_l = v / HG, head_l = v % HG;
+  const int tok_l = v >> a.hg_shift, head_l = v & (HG - 1);
   const int j = t.tt * TOK + tok_l;
   const int head = t.hg * HG + head_l;
   const bool vj = j < count;
@@ -338,7 +367,7 @@ __device__ __forceinline__ void issue_tile(const CompressArgs& a, const Tile& t,
     // clamped into the table: a position past it must not read outside the RoPE rows
     const int pos = vj ? min(max(a.positions ? a.positions[(int64_t)t.b * a.n_kept + j] : row, 0), a.rope_rows - 1)
                        : -1;
-    const int tw0 = wv0 / HG, ntw = (WV + HG - 1) / HG;  // tokens of this warp
+    const int tw0 = wv0 >> a.hg_shift, ntw = (WV + HG - 1) >> a.hg_shift;  // tokens of this warp
     const int n_chunks = ntw * 2 * HALF;
     for (int c0 = 0; c0 < n_chunks; c0 += 32) {  // uniform trip count: the shuffle needs every lane
       const int c = c0 + lane;
@@ -359,18 +388,18 @@ __device__ __forceinline__ void issue_tile(const CompressArgs& a, const Tile& t,
 // [h*DP/4, (h+1)*DP/4): all butterfly stages but one are in-thread, the stage
 // of stride DP/4 crosses the pair through one shuffle per register.
 // --------------------------------------------------------------------------
-template <typename TIn, int D, int DP, bool KEY, int FMT, bool RECON>
+template <typename TIn, int D, int DP, bool KEY, int LEV, bool RECON>
 __device__ __forceinline__ void compress_tile(const CompressArgs& a, const Tile& t, const uint8_t* stage) {
   using S = Smem<TIn, D>;
   constexpr int H2 = DP / 2;  // pairs per vector
   constexpr int HP = H2 / 2;  // pairs per thread
   const LayerIO& L = a.layers[t.layer];
   if ((KEY ? L.k : L.v) == nullptr) return;  // uniform over the CTA
-  const int levels = KEY ? L.key_levels : L.value_levels;
-  const int HG = a.head_group, TOK = kCompressVecs / HG;
+  constexpr int FMT = fmt_of(LEV);
+  const int HG = a.head_group, TOK = kCompressVecs >> a.hg_shift;
   const int count = a.kept_count ? min(a.kept_count[t.b], a.n_kept) : a.n_kept;
   const int v = threadIdx.x >> 1, h = threadIdx.x & 1;
-  const int tok_l = v / HG, head_l = v % HG;
+  const int tok_l = v >> a.hg_shift, head_l = v & (HG - 1);
   const int j = t.tt * TOK + tok_l;
   const int head = t.hg * HG + head_l;
   // both threads of every pair run the whole body (they exchange data); invalid ones store nothing
@@ -474,7 +503,7 @@ __device__ __forceinline__ void compress_tile(const CompressArgs& a, const Tile&
   }
   amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
   amax = fmaxf(amax, 1e-8f);
-  const float sc = __fmul_rn(amax, 2.0f / static_cast<float>(levels));
+  const float sc = __fmul_rn(amax, 2.0f / static_cast<float>(LEV));  // 2 / L: exact (power of two)
   const float rcp = __frcp_rn(sc);
   const u64 r2 = pk(rcp, rcp), nsc2 = pk(-sc, -sc);
 
@@ -498,8 +527,7 @@ __device__ __forceinline__ void compress_tile(const CompressArgs& a, const Tile&
       const u64 q1 = mul2(y, r2);
       const u64 rem = fma2(q1, nsc2, y);
       const u64 n = fma2(rem, r2, q1);
-      // the roundings run as scalar fp32 ops: unlike the packed ones they can issue to
-      // either FMA pipe, which balances the pipes here (measured ~4 % faster)
+      // the roundings run as scalar fp32 ops (packed forms measured no faster)
       float n0, n1;
       upk(n, n0, n1);
       const float s0 = __fadd_rn(n0, kMagic), s1 = __fadd_rn(n1, kMagic);
@@ -510,8 +538,8 @@ __device__ __forceinline__ void compress_tile(const CompressArgs& a, const Tile&
       blo[i] = __float_as_uint(b0); bhi[i] = __float_as_uint(b1);
     }
     uint32_t glo[GF<FMT>::kWords], ghi[GF<FMT>::kWords];
-    e8_group<FMT>(elo, slo, blo, levels, glo);
-    e8_group<FMT>(ehi, shi, bhi, levels, ghi);
+    e8_group<FMT, LEV>(elo, slo, blo, glo);
+    e8_group<FMT, LEV>(ehi, shi, bhi, ghi);
     place_group<FMT>(wl, g, glo);
     place_group<FMT>(wh, g, ghi);
     if constexpr (RECON) {
@@ -578,7 +606,7 @@ __device__ __forceinline__ void compress_tile(const CompressArgs& a, const Tile&
 // holds one per-vector body, half the code of a kernel that handles both, which keeps the
 // instruction cache from thrashing.
 // --------------------------------------------------------------------------
-template <typename TIn, int D, int DP, int FMTK, int FMTV, bool RECON, int KVS>
+template <typename TIn, int D, int DP, int LEV, bool RECON, int KVS>
 __global__ void __launch_bounds__(kCompressThreads, 4) compress_kernel(const CompressArgs args, int n_layers,
                                                                         int n_tiles, int ns) {
   using S = Smem<TIn, D>;
@@ -587,18 +615,19 @@ __global__ void __launch_bounds__(kCompressThreads, 4) compress_kernel(const Com
   if (first >= n_tiles) return;
   const int base = KVS * n_tiles;  // n_tiles = tiles of this half
   const int stage_bytes = S::stage(args.head_group);
-  Tile cur = decode_tile(args, n_layers, base + first);
+  const TileGeom geom = tile_geom(args);
+  const int step = (int)gridDim.x;
+  Tile cur = decode_tile(args, geom, n_layers, base + first);
   issue_tile<TIn, D>(args, cur, smem);
   cp_async_commit();
   int it = 0;
   // ns = 2: tile i+1 is copied into the other stage while tile i is computed;
   // ns = 1 (rows too large for two stages): copy and compute alternate.
-  for (int tile = first; tile < n_tiles; tile += gridDim.x, ++it) {
+  for (int tile = first; tile < n_tiles; tile += step, ++it) {
     const int s = ns == 2 ? (it & 1) : 0;
-    const int next = tile + (int)gridDim.x;
-    const bool has_next = next < n_tiles;
+    const bool has_next = tile + step < n_tiles;
     Tile nt = cur;
-    if (has_next) nt = decode_tile(args, n_layers, base + next);
+    if (has_next) advance_tile(nt, args, geom, step);
     if (ns == 2) {
       __syncwarp();  // this warp is done with stage s^1 (previous tile)
       if (has_next) issue_tile<TIn, D>(args, nt, smem + (s ^ 1) * stage_bytes);
@@ -609,8 +638,7 @@ __global__ void __launch_bounds__(kCompressThreads, 4) compress_kernel(const Com
     }
     __syncwarp();
     const uint8_t* stage = smem + s * stage_bytes;
-    if constexpr (KVS == 0) compress_tile<TIn, D, DP, true, FMTK, RECON>(args, cur, stage);
-    else compress_tile<TIn, D, DP, false, FMTV, RECON>(args, cur, stage);
+    compress_tile<TIn, D, DP, KVS == 0, LEV, RECON>(args, cur, stage);
     if (ns == 1 && has_next) {
       __syncwarp();
       issue_tile<TIn, D>(args, nt, smem);
@@ -623,8 +651,10 @@ __global__ void __launch_bounds__(kCompressThreads, 4) compress_kernel(const Com
 // --------------------------------------------------------------------------
 // Launch
 // --------------------------------------------------------------------------
-template <typename TIn, int D, int DP, int FMTK, int FMTV>
-static cudaError_t launch_fmt(const CompressArgs& a, int n_layers, long long n_tiles, cudaStream_t s, bool recon) {
+// One half of the tile list (kvs 0: key tiles, 1: value tiles) at level count LEV.
+template <typename TIn, int D, int DP, int LEV>
+static cudaError_t launch_half(const CompressArgs& a, int n_layers, long long half, int kvs, cudaStream_t s,
+                               bool recon) {
   using S = Smem<TIn, D>;
   int dev = 0, sms = 0, per_sm = 0, max_smem = 0;
   cudaError_t e;
@@ -632,44 +662,45 @@ static cudaError_t launch_fmt(const CompressArgs& a, int n_layers, long long n_t
   if ((e = cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess) return e;
   const int ns = 2 * (size_t)S::stage(a.head_group) + 64 <= (size_t)max_smem ? 2 : 1;
   const size_t smem = ns * (size_t)S::stage(a.head_group);
-  // key tiles (first half of the tile list), then value tiles, one kernel each
-  const long long half = n_tiles / 2;
-  for (int kvs = 0; kvs < 2; ++kvs) {
-    auto kern = kvs == 0 ? (recon ? compress_kernel<TIn, D, DP, FMTK, FMTV, true, 0>
-                                  : compress_kernel<TIn, D, DP, FMTK, FMTV, false, 0>)
-                         : (recon ? compress_kernel<TIn, D, DP, FMTK, FMTV, true, 1>
-                                  : compress_kernel<TIn, D, DP, FMTK, FMTV, false, 1>);
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
-    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kCompressThreads, smem)) != cudaSuccess)
-      return e;
-    long long grid = (long long)sms * (per_sm > 0 ? per_sm : 1);
-    if (grid > half) grid = half;
-    if (grid > 0) kern<<<(unsigned)grid, kCompressThreads, smem, s>>>(a, n_layers, (int)half, ns);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  }
+  auto kern = kvs == 0 ? (recon ? compress_kernel<TIn, D, DP, LEV, true, 0> : compress_kernel<TIn, D, DP, LEV, false, 0>)
+                       : (recon ? compress_kernel<TIn, D, DP, LEV, true, 1> : compress_kernel<TIn, D, DP, LEV, false, 1>);
+  if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) != cudaSuccess) return e;
+  if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kCompressThreads, smem)) != cudaSuccess)
+    return e;
+  long long grid = (long long)sms * (per_sm > 0 ? per_sm : 1);
+  if (grid > half) grid = half;
+  if (grid > 0) kern<<<(unsigned)grid, kCompressThreads, smem, s>>>(a, n_layers, (int)half, ns);
   return cudaGetLastError();
 }
 
 template <typename TIn, int D, int DP>
-static cudaError_t launch_dims(const CompressArgs& a, int n_layers, long long n_tiles, int fk, int fv,
+static cudaError_t launch_dims(const CompressArgs& a, int n_layers, long long n_tiles, int lk, int lv,
                                cudaStream_t s, bool recon) {
-#define NQ_FMT_CASE(K_, V_) \
-  if (fk == K_ && fv == V_) return launch_fmt<TIn, D, DP, K_, V_>(a, n_layers, n_tiles, s, recon);
-  NQ_FMT_CASE(0, 0) NQ_FMT_CASE(1, 0) NQ_FMT_CASE(1, 1) NQ_FMT_CASE(0, 1) NQ_FMT_CASE(2, 0) NQ_FMT_CASE(2, 1)
-  NQ_FMT_CASE(2, 2) NQ_FMT_CASE(0, 2) NQ_FMT_CASE(1, 2)
-#undef NQ_FMT_CASE
-  return cudaErrorInvalidValue;
+  // key tiles (first half of the tile list), then value tiles, one kernel each
+  const long long half = n_tiles / 2;
+  for (int kvs = 0; kvs < 2; ++kvs) {
+    const int lev = kvs == 0 ? lk : lv;
+    if (lev == 0) continue;  // no layer of this launch has this tensor
+    cudaError_t e = cudaErrorInvalidValue;
+    switch (lev) {
+      case 2: e = launch_half<TIn, D, DP, 2>(a, n_layers, half, kvs, s, recon); break;
+      case 4: e = launch_half<TIn, D, DP, 4>(a, n_layers, half, kvs, s, recon); break;
+      case 8: e = launch_half<TIn, D, DP, 8>(a, n_layers, half, kvs, s, recon); break;
+      case 16: e = launch_half<TIn, D, DP, 16>(a, n_layers, half, kvs, s, recon); break;
+    }
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 // Instantiated once per input dtype in nq_compress_{f16,bf16,f32}.cu (parallel builds).
 template <typename TIn>
-cudaError_t launch_compress_t(const CompressArgs& a, int n_layers, long long n_tiles, int fk, int fv, cudaStream_t s,
+cudaError_t launch_compress_t(const CompressArgs& a, int n_layers, long long n_tiles, int lk, int lv, cudaStream_t s,
                               bool recon) {
-  if (a.head_dim == 128 && a.head_dim_padded == 128) return launch_dims<TIn, 128, 128>(a, n_layers, n_tiles, fk, fv, s, recon);
-  if (a.head_dim == 96 && a.head_dim_padded == 128) return launch_dims<TIn, 96, 128>(a, n_layers, n_tiles, fk, fv, s, recon);
-  if (a.head_dim == 64 && a.head_dim_padded == 64) return launch_dims<TIn, 64, 64>(a, n_layers, n_tiles, fk, fv, s, recon);
+  if (a.head_dim == 128 && a.head_dim_padded == 128) return launch_dims<TIn, 128, 128>(a, n_layers, n_tiles, lk, lv, s, recon);
+  if (a.head_dim == 96 && a.head_dim_padded == 128) return launch_dims<TIn, 96, 128>(a, n_layers, n_tiles, lk, lv, s, recon);
+  if (a.head_dim == 64 && a.head_dim_padded == 64) return launch_dims<TIn, 64, 64>(a, n_layers, n_tiles, lk, lv, s, recon);
   return cudaErrorInvalidValue;
 }
 

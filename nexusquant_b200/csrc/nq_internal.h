@@ -27,6 +27,7 @@ struct LayerIO {
 struct CompressArgs {
   int32_t batch, heads, seq, head_dim, head_dim_padded, n_kept;
   int32_t head_group;  // heads per CTA tile (1, 2, 4 or 8)
+  int32_t hg_shift;    // log2(head_group), set by launch_compress
   const int32_t* kept_idx;
   const int32_t* kept_count;
   const int32_t* positions;
