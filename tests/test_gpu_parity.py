@@ -186,6 +186,24 @@ def test_no_rotation_mode_matches_quantize_perhead(orc):
     assert np.array_equal(q, ref)
 
 
+@pytest.mark.parametrize("levels", [2, 4, 8, 16])
+def test_step_direction_at_tiny_gaps(orc, levels):
+    """The A step moves toward x (e8_lattice.py:42-43) even where fl(x - 1/2) rounds onto a
+    half-way point: x just below 0 (a = 0, e < 0) and x = -1 + 2^-24 (a = -1, e > 0), each the
+    smallest gap of an odd-sum group that keeps the integer candidate."""
+    half = levels / 2
+    g1 = [-1e-9, 0.1, 0.1, 0.1, 0.9, 0.1, 0.1, 0.1]
+    g2 = [-1.0 + 2.0 ** -24, 0.1, 0.1, 0.1, 0.1, 0.1, 0.1, 0.1]
+    row = np.zeros(128, np.float32)
+    row[0:8], row[8:16], row[16] = g1, g2, half  # amax = L/2: scale 1, x / scale = x
+    x = torch.from_numpy(np.stack([row, -row, row[::-1].copy()]))
+    codes, scales = K.e8_encode(x.to(DEV), levels=levels)
+    oc, osc = orc.quantize(x.numpy(), 128, levels, rotate=False)
+    assert np.array_equal(scales.cpu().numpy(), osc)
+    assert np.array_equal(codes.cpu().numpy(), oc)
+    assert oc[0, 0] == -2 and oc[0, 8] == 0  # stepped down from 0, up from -1
+
+
 # ----------------------------------------------------------------- scoring + select
 def test_keykey_importance_vs_oracle_and_reference(golden, orc):
     cfg = syn.CacheConfig("score", 1, 2, 4, 300, 128)
@@ -395,6 +413,21 @@ def test_attend_compressed_vs_decompress_then_attention(orc, lk, lv, g, sharpen)
     assert rel_l2(got.cpu().numpy(), ref.cpu().numpy()) < REL_L2_TOL
     again = K.attend_compressed(q, lc, pos, count=count, key_sharpen=sharpen)
     assert torch.equal(got, again)  # deterministic
+
+
+def test_attend_compressed_empty_layer_zeroes_strided_output():
+    """No stored tokens: every query row of a strided output is zeroed, and nothing else."""
+    codes = K.LayerCodes(torch.zeros((2, 2, 0, 64), dtype=torch.uint8, device=DEV),
+                         torch.zeros((2, 2, 0, 64), dtype=torch.uint8, device=DEV),
+                         torch.zeros((2, 2, 0), dtype=torch.float16, device=DEV),
+                         torch.zeros((2, 2, 0), dtype=torch.float16, device=DEV), 4, 4)
+    q = torch.ones((2, 4, 128), dtype=torch.float16, device=DEV)
+    big = torch.full((2, 5, 160), 7.0, dtype=torch.float16, device=DEV)   # rows of 160, 5 per batch
+    out = big[:, :4, :128]
+    K.attend_compressed(q, codes, torch.zeros((2, 0), dtype=torch.int32, device=DEV), out=out, rope_rows=1)
+    torch.cuda.synchronize()
+    assert torch.count_nonzero(out) == 0
+    assert bool((big[:, 4] == 7).all()) and bool((big[:, :4, 128:] == 7).all())
 
 
 def test_positions_past_the_rope_table_are_clamped():
