@@ -319,13 +319,9 @@ nq_status_t nq_attend_compressed(const nq_attend_params_t* p, void* workspace, s
   if (g != 1 && g != 2 && g != 4 && g != 8) return NQ_ERR_UNSUPPORTED;
   if (!valid_levels(p->key_levels) || !valid_levels(p->value_levels)) return NQ_ERR_INVALID_ARG;
   if (p->batch == 0) return NQ_OK;
-  if (!p->q || !p->out || !p->k_codes || !p->v_codes || !p->k_scales || !p->v_scales || !p->positions ||
-      !p->rope_cos || !p->rope_sin || p->rope_rows <= 0)
-    return NQ_ERR_INVALID_ARG;
-  const void* al[] = {p->k_codes, p->v_codes, p->rope_cos, p->rope_sin};
-  for (const void* q : al)
-    if (!aligned16(q)) return NQ_ERR_ALIGNMENT;
   if (p->n_tokens == 0) {
+    // empty code tensors may carry null pointers: only the output is needed
+    if (!p->out) return NQ_ERR_INVALID_ARG;
     // nothing to attend: zero the [q_heads, 128] fp16 rows of each batch element (one strided
     // memset per batch element)
     if (p->out_stride_h < 128) return NQ_ERR_INVALID_ARG;
@@ -336,6 +332,12 @@ nq_status_t nq_attend_compressed(const nq_attend_params_t* p, void* workspace, s
     }
     return NQ_OK;
   }
+  if (!p->q || !p->out || !p->k_codes || !p->v_codes || !p->k_scales || !p->v_scales || !p->positions ||
+      !p->rope_cos || !p->rope_sin || p->rope_rows <= 0)
+    return NQ_ERR_INVALID_ARG;
+  const void* al[] = {p->k_codes, p->v_codes, p->rope_cos, p->rope_sin};
+  for (const void* q : al)
+    if (!aligned16(q)) return NQ_ERR_ALIGNMENT;
   const int splits = nq::attend_splits(p->batch, p->heads, p->n_tokens);
   if (!workspace || workspace_bytes < nq::attend_workspace_bytes(p->batch, p->q_heads, splits))
     return NQ_ERR_WORKSPACE;

@@ -255,7 +255,11 @@ static cudaError_t score_dim(const ScoreArgs& a, float* colsum, void* ws, cudaSt
 }
 
 cudaError_t launch_score_colsums(const ScoreArgs& a, float* colsum, void* ws, size_t, cudaStream_t s) {
-  if (score_umma_supported(a)) return launch_score_umma(a, colsum, ws, s);
+  if (score_umma_supported(a)) {
+    // cudaErrorNotSupported: the tensor maps could not be encoded; nothing was launched
+    const cudaError_t e = launch_score_umma(a, colsum, ws, s);
+    if (e != cudaErrorNotSupported) return e;
+  }
   switch (a.in_dtype) {
     case 0: return score_dim<__half>(a, colsum, ws, s);
     case 1: return score_dim<__nv_bfloat16>(a, colsum, ws, s);

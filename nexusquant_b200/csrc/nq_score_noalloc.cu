@@ -17,6 +17,10 @@
 //    be serialised by the caller.
 //  - The kernels fully overwrite the scratch they read (tile maxima and sums,
 //    row statistics, per-head column sums), so nothing is cleared between calls.
+//  - The address is cached per device ordinal for the life of the process.  A
+//    cudaDeviceReset (or anything else that destroys and recreates the device's
+//    primary context) makes the cached address stale: callers that reset a device
+//    must not call this entry point on it afterwards.
 #include <cmath>
 #include <mutex>
 

@@ -397,15 +397,16 @@ cudaError_t run_umma(const ScoreArgs& a, float* colsum, void* ws, cudaStream_t s
   UmWs w{reinterpret_cast<float*>(p), reinterpret_cast<float*>(p + part), reinterpret_cast<float*>(p + 2 * part),
          reinterpret_cast<float*>(p + 2 * part + stat)};
   CUtensorMap kmap, qmap;
+  // a layout the tensor-map encoder refuses (extents, strides) goes to the CUDA-core scorer
   if (!make_map(&kmap, a.k, a.in_dtype, D, a.seq, a.heads, a.batch, a.k_stride_t, a.k_stride_h, a.k_stride_b,
                 kUmKeys))
-    return cudaErrorInvalidValue;
+    return cudaErrorNotSupported;
   const bool qmap_ok =
       a.q ? make_map(&qmap, a.q, a.in_dtype, D, a.n_q, a.q_heads, a.batch, a.q_stride_t, a.q_stride_h, a.q_stride_b,
                      NQP)
           : make_map(&qmap, a.k, a.in_dtype, D, a.seq, a.heads, a.batch, a.k_stride_t, a.k_stride_h, a.k_stride_b,
                      NQP);
-  if (!qmap_ok) return cudaErrorInvalidValue;
+  if (!qmap_ok) return cudaErrorNotSupported;
   int dev = 0, sms = 0;
   cudaError_t e;
   if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;

@@ -16,6 +16,8 @@
 //     chunks of 4096 tokens with block scans, writing at its own offset.
 #include <cooperative_groups.h>
 
+#include <mutex>
+
 #include "nq_common.cuh"
 #include "nq_internal.h"
 
@@ -304,10 +306,20 @@ static cudaError_t launch_cs(const float* imp, int batch, int seq, int sw, int n
 }
 
 // 16 CTAs per row where the device schedules clusters of 16 (a non-portable size), else 8.
+// The attribute that allows the size is set per device, so the answer is cached per device
+// ordinal, each entry set once under a mutex (several host threads may select at once).
 static bool cluster16_ok() {
-  static int ok = -1;
-  if (ok < 0) {
-    ok = 0;
+  constexpr int kMaxDev = 64;
+  static std::mutex mu;
+  static signed char ok[kMaxDev] = {};  // 0 unknown, 1 yes, -1 no
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) {
+    cudaGetLastError();
+    return false;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (ok[dev] == 0) {
+    ok[dev] = -1;
     if (cudaFuncSetAttribute(select_kernel<16>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(16);
@@ -320,11 +332,12 @@ static bool cluster16_ok() {
       cfg.attrs = attr;
       cfg.numAttrs = 1;
       int clusters = 0;
-      if (cudaOccupancyMaxActiveClusters(&clusters, select_kernel<16>, &cfg) == cudaSuccess && clusters > 0) ok = 1;
+      if (cudaOccupancyMaxActiveClusters(&clusters, select_kernel<16>, &cfg) == cudaSuccess && clusters > 0)
+        ok[dev] = 1;
     }
     cudaGetLastError();
   }
-  return ok == 1;
+  return ok[dev] == 1;
 }
 
 cudaError_t launch_select(const float* imp, int batch, int seq, int sw, int n_keep, const int32_t* prot, int n_prot,

@@ -18,24 +18,29 @@ pytestmark = pytest.mark.gpu
 DEV = "cuda:0"
 
 
+_CODE = {torch.float16: 0, torch.bfloat16: 1, torch.float32: 2}
+
+
 def _reference_scores(lib, k, per_head, h0, h1):
     b, h, T, d = k.shape
+    dt = _CODE[k.dtype]
     ws_n = lib.nq_score_keykey_workspace_size(b, h1 - h0, T, 32)
     ws = torch.empty(ws_n, dtype=torch.uint8, device=DEV)
     out = torch.empty((b, h1 - h0, T) if per_head else (b, T), dtype=torch.float32, device=DEV)
     st = k.stride()
     s = torch.cuda.current_stream().cuda_stream
-    N.check("nq_score_keykey", lib.nq_score_keykey(k.data_ptr(), 0, b, h, T, d, st[0], st[1], st[2], 32, h0, h1,
+    N.check("nq_score_keykey", lib.nq_score_keykey(k.data_ptr(), dt, b, h, T, d, st[0], st[1], st[2], 32, h0, h1,
                                                    int(per_head), out.data_ptr(), ws.data_ptr(), ws_n, s))
     return out
 
 
 def _noalloc_scores(lib, k, per_head, h0, h1):
     b, h, T, d = k.shape
+    dt = _CODE[k.dtype]
     out = torch.empty((b, h1 - h0, T) if per_head else (b, T), dtype=torch.float32, device=DEV)
     st = k.stride()
     s = torch.cuda.current_stream().cuda_stream
-    N.check("nq_score_keykey_noalloc", lib.nq_score_keykey_noalloc(k.data_ptr(), 0, b, h, T, d, st[0], st[1],
+    N.check("nq_score_keykey_noalloc", lib.nq_score_keykey_noalloc(k.data_ptr(), dt, b, h, T, d, st[0], st[1],
                                                                    st[2], 32, h0, h1, int(per_head),
                                                                    out.data_ptr(), s))
     return out
@@ -50,6 +55,32 @@ def test_noalloc_matches_workspace_entry_two_calls(per_head, h0, h1):
         k = k.to(DEV)
         ref = _reference_scores(lib, k, per_head, h0, h1)
         got = _noalloc_scores(lib, k, per_head, h0, h1)
+        torch.cuda.synchronize()
+        assert np.allclose(got.cpu().numpy(), ref.cpu().numpy(), rtol=5e-5, atol=1e-8)
+
+
+@pytest.mark.parametrize("dtype,d", [(torch.float32, 128), (torch.bfloat16, 96), (torch.float16, 64),
+                                     (torch.float32, 96)])
+def test_noalloc_other_dtypes_and_head_dims(dtype, d):
+    """fp32 runs the CUDA-core scorer, fp16/bf16 the tensor-core one; both carve the same array."""
+    lib = N.load()
+    for layer, seq in ((2, 2048), (3, 777)):
+        k, _ = syn.cpu_layer(syn.CacheConfig("na", 1, 2, 4, seq, d), layer)
+        k = k.to(DEV, dtype)
+        ref = _reference_scores(lib, k, 0, 0, 4)
+        got = _noalloc_scores(lib, k, 0, 0, 4)
+        torch.cuda.synchronize()
+        assert np.allclose(got.cpu().numpy(), ref.cpu().numpy(), rtol=5e-5, atol=1e-8)
+
+
+def test_noalloc_at_documented_capacity():
+    """One 131072-token, 8-head, head_dim-128 layer fits in the built-in scratch (6 MiB of 8)."""
+    lib = N.load()
+    g = torch.Generator(device=DEV).manual_seed(5)
+    for _ in range(2):
+        k = torch.randn((1, 8, 131072, 128), generator=g, device=DEV).half()
+        ref = _reference_scores(lib, k, 0, 0, 8)
+        got = _noalloc_scores(lib, k, 0, 0, 8)
         torch.cuda.synchronize()
         assert np.allclose(got.cpu().numpy(), ref.cpu().numpy(), rtol=5e-5, atol=1e-8)
 
