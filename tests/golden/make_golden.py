@@ -125,16 +125,44 @@ def make_merge(P) -> dict:
     return fx
 
 
+def entropy_coords():
+    """Seeded int8 lattice codes with temporal correlation (a random walk along 96 tokens of
+    16 streams x 128 coordinates, clipped to [-4, 4]); regenerated bit-identically by the tests."""
+    rng = np.random.default_rng(20240601)
+    steps = rng.integers(-1, 2, size=(96, 16 * 128))
+    return np.clip(np.cumsum(steps, axis=0), -4, 4).astype(np.int8).reshape(-1), 96
+
+
+def make_entropy() -> dict:
+    """temporal_codec.compress_indices (temporal_codec.py:76-106) run by the reference itself, with
+    and without the temporal delta.  Without the zstandard module the reference writes zlib
+    streams (compressor 0), which is what a container without it records."""
+    from nexusquant.core import temporal_codec as TC
+    coords, n_tokens = entropy_coords()
+    fx = {"coords_sha": np.frombuffer(sha(coords).encode(), np.uint8), "n_tokens": np.int64(n_tokens),
+          "has_zstd": np.int64(int(TC._HAS_ZSTD))}
+    for use_delta in (True, False):
+        blob = TC.compress_indices(coords, n_tokens, use_delta=use_delta)
+        fx[f"stream_delta{int(use_delta)}"] = np.frombuffer(blob, np.uint8)
+        fx[f"delta{int(use_delta)}_roundtrip"] = np.int64(int(np.array_equal(TC.decompress_indices(blob), coords)))
+    return fx
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("NQ_REFERENCE"),
                     help="checkout of the reference (or set NQ_REFERENCE)")
-    ap.add_argument("--part", choices=["all", "merge"], default="all",
-                    help="merge: write only merge.npz (merge eviction fixtures)")
+    ap.add_argument("--part", choices=["all", "merge", "entropy"], default="all",
+                    help="merge: write only merge.npz (merge eviction fixtures); entropy: only entropy.npz")
     args = ap.parse_args()
     if not args.ref:
         ap.error("--ref (or NQ_REFERENCE) must name the reference checkout")
     sys.path.insert(0, args.ref)
+    if args.part == "entropy":
+        out = os.path.join(HERE, "entropy.npz")
+        np.savez_compressed(out, **make_entropy())
+        print("wrote", out, os.path.getsize(out), "bytes")
+        return
     if args.part == "merge":
         from nexusquant import pipeline as P
         torch.set_num_threads(8)
@@ -375,6 +403,9 @@ def main():
     print("wrote", out, os.path.getsize(out), "bytes")
     out = os.path.join(HERE, "merge.npz")
     np.savez_compressed(out, **make_merge(P))
+    print("wrote", out, os.path.getsize(out), "bytes")
+    out = os.path.join(HERE, "entropy.npz")
+    np.savez_compressed(out, **make_entropy())
     print("wrote", out, os.path.getsize(out), "bytes")
 
 
