@@ -98,7 +98,7 @@ __device__ __forceinline__ void e8_group(const float (&e)[8], const uint32_t (&s
   const uint32_t km = in_hi ? kh : kl;
   const uint32_t gbits = km >> 2;
   const int idx = (in_hi ? 4 : 0) + (int)(km & 3u);
-  // Sign bits of e (bit 7 - i for coordinate i), for the direction of the A step.
+  // sign bits of e (bit 7 - i for coordinate i), for the direction of the A step
   uint32_t neg = 0u;
 #pragma unroll
   for (int i = 0; i < 8; ++i) neg = __funnelshift_l(__float_as_uint(e[i]), neg, 1);
@@ -118,7 +118,9 @@ __device__ __forceinline__ void e8_group(const float (&e)[8], const uint32_t (&s
   const bool use_b = lhs > 2.0f;
 
   // A step at coordinate idx: one step toward x, up when e_idx >= 0 (e8_lattice.py:42-43;
-  // e = -0 only for x = -0, whose gap is 0 and which steps up)
+  // e = -0 only for x = -0, whose gap is 0 and which steps up).  The sign is read from e
+  // itself: the B field (fA + 1 for e > 0, fA - 1 for e < 0) says otherwise where fl(x - 1/2)
+  // rounded onto a half-way point (x just below 0, x = -1 + 2^-24).
   const int sh = F::kWidth * (FMT == 0 ? idx : (idx & 3));
   const uint32_t wa_i = (NW == 1 || idx < 4) ? wa[0] : wa[NW - 1];
   const uint32_t fa = (wa_i >> sh) & F::kMask;
@@ -527,13 +529,16 @@ __device__ __forceinline__ void compress_tile(const CompressArgs& a, const Tile&
       const u64 q1 = mul2(y, r2);
       const u64 rem = fma2(q1, nsc2, y);
       const u64 n = fma2(rem, r2, q1);
-      // the roundings run as scalar fp32 ops (packed forms measured no faster)
-      float n0, n1;
-      upk(n, n0, n1);
-      const float s0 = __fadd_rn(n0, kMagic), s1 = __fadd_rn(n1, kMagic);
-      elo[i] = __fsub_rn(n0, __fsub_rn(s0, kMagic));
-      ehi[i] = __fsub_rn(n1, __fsub_rn(s1, kMagic));
-      const float b0 = __fadd_rn(__fsub_rn(n0, 0.5f), kMagic), b1 = __fadd_rn(__fsub_rn(n1, 0.5f), kMagic);
+      // the roundings, packed: s = n + M (rint in the low bits), e = n - (s - M), and
+      // b = fl(n - 1/2) + M for the half-integer candidate
+      const u64 M2 = pk(kMagic, kMagic);
+      const u64 s2 = add2(n, M2);
+      const u64 e2 = sub2(n, sub2(s2, M2));
+      const u64 b2 = add2(sub2(n, pk(0.5f, 0.5f)), M2);
+      float s0, s1, b0, b1;
+      upk(s2, s0, s1);
+      upk(e2, elo[i], ehi[i]);
+      upk(b2, b0, b1);
       slo[i] = __float_as_uint(s0); shi[i] = __float_as_uint(s1);
       blo[i] = __float_as_uint(b0); bhi[i] = __float_as_uint(b1);
     }

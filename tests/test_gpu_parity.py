@@ -202,6 +202,13 @@ def test_step_direction_at_tiny_gaps(orc, levels):
     assert np.array_equal(scales.cpu().numpy(), osc)
     assert np.array_equal(codes.cpu().numpy(), oc)
     assert oc[0, 0] == -2 and oc[0, 8] == 0  # stepped down from 0, up from -1
+    # many such rows: more flagged vectors than a CTA queues, so whole shares are redone exactly
+    xs = torch.from_numpy(np.tile(np.stack([row, -row, row[::-1].copy()]), (70, 1)))
+    xs[1::3] *= torch.linspace(0.5, 2.0, xs[1::3].shape[0])[:, None]
+    codes, scales = K.e8_encode(xs.to(DEV), levels=levels)
+    oc, osc = orc.quantize(xs.numpy(), 128, levels, rotate=False)
+    assert np.array_equal(scales.cpu().numpy(), osc)
+    assert np.array_equal(codes.cpu().numpy(), oc)
 
 
 # ----------------------------------------------------------------- scoring + select
