@@ -1,5 +1,5 @@
 #!/usr/bin/env python3
-"""Benchmark: post-prefill KV-cache compression on B200, sharded by layer.
+"""Benchmark: post-prefill KV-cache compression on B200, sharded across the GPUs of one node.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 4]
 
@@ -7,15 +7,22 @@ Workload (default): BASELINE config 4 -- Llama-3-70B-shaped 128K cache, 80 layer
 x 8 KV heads x head_dim 128, batch 1, T=131072, fp16 (42.95 GB of K+V), RoPE base
 5e5, 'max' preset: K2V2 + 80 % eviction with the key-key scorer on layer 0,
 first/last 2 layers protected at fp16.  Synthetic data (seeded N(0,1) keys with
-outlier channels + RoPE, N(0,1) values), generated on the device.
+outlier channels + RoPE, N(0,1) values), generated on the device.  ``--config 2``
+runs the real-attention scorer over every layer's 64 synthetic queries instead.
 
-One step = score layer 0 (each rank scores its share of the heads; per-head
-column sums are all-gathered over NCCL) -> keep set -> compress every layer the
-rank owns (one launch) + fp16 gather of its protected layers -> all-gather of
-per-layer compressed sizes.  Layers are assigned to ranks by cost (strong
-scaling: the cache is fixed, N GPUs share it).  value = fp16-in bytes of the
-whole cache / max-over-ranks step time.  Inputs (42.95 GB) are far larger than
-L2, so no flush is needed between steps.
+One step = score (each rank scores its block of KV heads; per-head column sums are
+all-gathered over NCCL, or for the real scorer the per-rank sums are all-reduced) ->
+keep set -> compress every (layer, head slice) the rank owns (one launch per half) +
+fp16 gather of its share of the protected layers -> all-gather of the per-layer
+compressed sizes.  With N dividing the KV heads each rank owns N-th of the heads of every
+layer (strong scaling: the cache is fixed, N GPUs share it).  value = fp16-in bytes of the
+whole cache / max-over-ranks step time.  Inputs are far larger than L2, so no flush is
+needed between steps.
+
+The same JSON line carries the kernel-only compress and dequantize rooflines of this
+configuration and (on one GPU) of configs 1-3, the end-to-end number through
+``NexusQuantEvict(layout="compressed")`` on a cache in pinned host memory, the CPU
+baseline, and the entropy-coded size (zstd host post-step, outside the timed region).
 """
 from __future__ import annotations
 
@@ -33,10 +40,11 @@ import torch.distributed as dist
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
+from nexusquant_b200 import entropy as E  # noqa: E402
 from nexusquant_b200 import kernels as K  # noqa: E402
 from nexusquant_b200 import sharding as S  # noqa: E402
 from nexusquant_b200 import synthetic as syn  # noqa: E402
-from nexusquant_b200.pipeline import kept_capacity, n_keep_for  # noqa: E402
+from nexusquant_b200.pipeline import NexusQuantEvict, kept_capacity, n_keep_for  # noqa: E402
 
 METRIC = "KV compress GB/s (fp16 in) & dequant GB/s, % of HBM peak, at 1/2/4/8 B200"
 
@@ -48,6 +56,33 @@ def peaks():
         return float(p["hbm_gbs"]), "measured"
     except Exception:
         return 6650.0, "fallback"
+
+
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def config_dict(cfg, cap: int, world: int) -> dict:
+    """The workload description, identical in both arms' lines."""
+    return {"workload": cfg.name, "layers": cfg.n_layers, "batch": cfg.batch, "heads": cfg.heads,
+            "seq": cfg.seq, "head_dim": cfg.head_dim, "key_bits": cfg.key_bits, "value_bits": cfg.value_bits,
+            "eviction_rate": cfg.eviction_rate, "scorer": cfg.scorer if cfg.eviction_rate > 0 else "none",
+            "kept_tokens": cap, "protected_layers": sorted(S.protected_layers(cfg.n_layers, cfg.protect_boundary)),
+            "parallelism": f"head-sharded x{world}" if cfg.heads % world == 0 else f"layer-sharded x{world}",
+            "l2": f"inputs ({cfg.fp16_bytes / 1e9:.2f} GB) larger than L2; no flush"}
+
+
+def cap_for(cfg) -> int:
+    if cfg.eviction_rate <= 0:
+        return cfg.seq
+    return kept_capacity(cfg.seq, cfg.sliding_window, n_keep_for(cfg.seq, cfg.sliding_window, cfg.eviction_rate))
 
 
 # ------------------------------------------------------------------ clocks (NVML)
@@ -105,99 +140,6 @@ class ClockSampler:
                 "reasons": [n for b, n in self.REASONS.items() if self.reasons & b]}
 
 
-# -------------------------------------------------------------------------- shard
-class Shard:
-    """One rank's part of the compression of a config-4-shaped cache."""
-
-    def __init__(self, cfg, rank: int, world: int, device, group=None):
-        self.cfg, self.rank, self.world, self.dev, self.group = cfg, rank, world, device, group
-        L = cfg.n_layers
-        self.plan = S.make_plan(L, cfg.heads, cfg.protect_boundary, rank, world)
-        self.owned = list(self.plan.layers)
-        self.quant = list(self.plan.quantized)
-        self.prot = list(self.plan.protected)
-        self.protected = S.protected_layers(L, cfg.protect_boundary)
-        h = cfg.heads
-        self.h0, self.h1, self.per = self.plan.head_begin, self.plan.head_end, self.plan.heads_per_rank
-        self.nk = n_keep_for(cfg.seq, cfg.sliding_window, cfg.eviction_rate)
-        self.cap = kept_capacity(cfg.seq, cfg.sliding_window, self.nk)
-        # resident data: this rank's layers, plus layer 0's keys for scoring
-        self.K, self.V = {}, {}
-        for l in self.owned:
-            self.K[l], self.V[l] = syn.device_layer(cfg, l, device)
-        self.K0 = self.K[0] if 0 in self.K else syn.device_layer(cfg, 0, device)[0]
-        b, _, T, d = self.K0.shape
-        dp = K.next_pow2(d)
-        self.levels = (2 ** cfg.key_bits, 2 ** cfg.value_bits)
-        n = self.cap
-        self.codes = [K.LayerCodes(
-            torch.empty((b, h, n, K.packed_bytes(dp, self.levels[0])), dtype=torch.uint8, device=device),
-            torch.empty((b, h, n, K.packed_bytes(dp, self.levels[1])), dtype=torch.uint8, device=device),
-            torch.empty((b, h, n), dtype=torch.float16, device=device),
-            torch.empty((b, h, n), dtype=torch.float16, device=device), *self.levels) for _ in self.quant]
-        self.prot_out = {l: (torch.empty((b, h, n, d), dtype=torch.float16, device=device),
-                             torch.empty((b, h, n, d), dtype=torch.float16, device=device)) for l in self.prot}
-        self.gathered = torch.empty((world * b * self.per, T), dtype=torch.float32, device=device)
-        pkv = K.packed_bytes(dp, self.levels[0]) + K.packed_bytes(dp, self.levels[1]) + 4
-        self.sizes = S.local_layer_sizes(self.plan, [b * h * n * pkv] * len(self.quant),
-                                         [2 * b * h * n * d * 2] * len(self.prot), device=device)
-        self.sizes_all = torch.zeros((world * L,), dtype=torch.int64, device=device)
-        self.launches = 0
-
-    # bytes
-    def fp16_in_bytes_total(self) -> int:
-        return self.cfg.fp16_bytes
-
-    def compress_algo_bytes(self) -> int:
-        """Algorithmic bytes of this rank's compress launch: read 2*d bytes per kept K and V
-        row, write packed codes + fp16 scale per row, read the kept index per (row, head) once."""
-        b, h, d = self.cfg.batch, self.cfg.heads, self.cfg.head_dim
-        dp = K.next_pow2(d)
-        pk, pv = K.packed_bytes(dp, self.levels[0]), K.packed_bytes(dp, self.levels[1])
-        rows = len(self.quant) * b * h * self.cap
-        return rows * (2 * d * 2 + pk + pv + 4)
-
-    def step(self):
-        cfg = self.cfg
-        b, h, T = cfg.batch, cfg.heads, cfg.seq
-        # global index of the compressed cache: the per-layer byte sizes of fixed-capacity
-        # outputs are known up front, so their exchange overlaps scoring and compression
-        _, sizes_work = S.gather_layer_index(self.sizes, self.plan, self.group, self.sizes_all, async_op=True)
-        if self.h1 > self.h0:
-            ph = K.score_keykey(self.K0, 32, head_range=(self.h0, self.h1), per_head=True)
-            self.launches += 3
-        else:
-            ph = torch.zeros((b, 0, T), dtype=torch.float32, device=self.dev)
-        allh = S.gather_head_scores(ph, self.plan, self.group, self.gathered)
-        imp = K.reduce_heads(allh, float(h))
-        idx, cnt = K.select_keep(imp, cfg.sliding_window, self.nk)
-        self.launches += 2
-        if self.quant:
-            K.compress_layers([self.K[l] for l in self.quant], [self.V[l] for l in self.quant],
-                              key_levels=self.levels[0], value_levels=self.levels[1], kept_idx=idx[:, :self.cap],
-                              kept_count=cnt, n_kept=self.cap, rope_base=cfg.rope_base, rope_rows=T,
-                              codes_out=self.codes)
-            self.launches += 2 * math.ceil(len(self.quant) / 96)  # key and value kernels
-        for l in self.prot:
-            K.gather_rows(self.K[l], idx[:, :self.cap], self.cap, cnt, out=self.prot_out[l][0])
-            K.gather_rows(self.V[l], idx[:, :self.cap], self.cap, cnt, out=self.prot_out[l][1])
-            self.launches += 2
-        self.kept_idx, self.kept_count = idx, cnt
-        if sizes_work is not None:
-            sizes_work.wait()
-
-    def compress_only(self):
-        K.compress_layers([self.K[l] for l in self.quant], [self.V[l] for l in self.quant],
-                          key_levels=self.levels[0], value_levels=self.levels[1],
-                          kept_idx=self.kept_idx[:, :self.cap], kept_count=self.kept_count, n_kept=self.cap,
-                          rope_base=self.cfg.rope_base, rope_rows=self.cfg.seq, codes_out=self.codes)
-
-    def dequant(self, outs):
-        return K.decompress_layers(self.codes, self.kept_idx[:, :self.cap], head_dim=self.cfg.head_dim,
-                                   count=self.kept_count, rope_base=self.cfg.rope_base, out_k=outs[0],
-                                   out_v=outs[1])
-
-
 def timed(fn, steps, warmup, world, group=None):
     for _ in range(warmup):
         fn()
@@ -219,6 +161,180 @@ def timed(fn, steps, warmup, world, group=None):
         ms = float(t.item())
         dist.barrier(group=group)
     return ms
+
+
+# -------------------------------------------------------------------------- shard
+class Shard:
+    """One rank's part of the compression of a benchmark cache."""
+
+    def __init__(self, cfg, rank: int, world: int, device, group=None):
+        self.cfg, self.rank, self.world, self.dev, self.group = cfg, rank, world, device, group
+        L, h = cfg.n_layers, cfg.heads
+        self.plan = S.make_plan(L, h, cfg.protect_boundary, rank, world)
+        self.owned = list(self.plan.layers)
+        self.quant = list(self.plan.quantized)
+        self.prot = list(self.plan.protected)
+        self.protected = S.protected_layers(L, cfg.protect_boundary)
+        self.lh0, self.lh1 = self.plan.layer_heads      # heads of each owned layer
+        self.hl = self.lh1 - self.lh0
+        self.h0, self.h1, self.per = self.plan.head_begin, self.plan.head_end, self.plan.heads_per_rank
+        self.real = cfg.scorer == "real" and cfg.eviction_rate > 0
+        self.nk = n_keep_for(cfg.seq, cfg.sliding_window, cfg.eviction_rate)
+        self.cap = cap_for(cfg)
+        b, T, d = cfg.batch, cfg.seq, cfg.head_dim
+        # resident data: this rank's head slice of its layers
+        self.K, self.V, self.Q = {}, {}, {}
+        for l in self.owned:
+            k, v = syn.device_layer(cfg, l, device)
+            self.K[l], self.V[l] = self._slice(k), self._slice(v)
+            del k, v
+            if self.real:
+                self.Q[l] = self._slice(syn.device_queries(cfg, l, device))
+        if self.real or cfg.eviction_rate <= 0:
+            self.K0 = None
+        elif self.plan.mode == "heads":
+            self.K0 = self.K[0]  # the scored block is this rank's slice of layer 0
+        else:
+            k0 = self.K[0] if 0 in self.K else syn.device_layer(cfg, 0, device)[0]
+            self.K0 = k0[:, self.h0:self.h1].contiguous() if self.h1 > self.h0 else None
+        dp = K.next_pow2(d)
+        self.levels = (2 ** cfg.key_bits, 2 ** cfg.value_bits)
+        n = self.cap
+        self.codes = [K.LayerCodes(
+            torch.empty((b, self.hl, n, K.packed_bytes(dp, self.levels[0])), dtype=torch.uint8, device=device),
+            torch.empty((b, self.hl, n, K.packed_bytes(dp, self.levels[1])), dtype=torch.uint8, device=device),
+            torch.empty((b, self.hl, n), dtype=torch.float16, device=device),
+            torch.empty((b, self.hl, n), dtype=torch.float16, device=device), *self.levels) for _ in self.quant]
+        self.prot_out = {l: (torch.empty((b, self.hl, n, d), dtype=torch.float16, device=device),
+                             torch.empty((b, self.hl, n, d), dtype=torch.float16, device=device)) for l in self.prot}
+        self.gathered = torch.empty((world * b * self.per, T), dtype=torch.float32, device=device)
+        pkv = K.packed_bytes(dp, self.levels[0]) + K.packed_bytes(dp, self.levels[1]) + 4
+        self.sizes = S.local_layer_sizes(self.plan, [b * self.hl * n * pkv] * len(self.quant),
+                                         [2 * b * self.hl * n * d * 2] * len(self.prot), device=device)
+        self.sizes_all = torch.zeros((world * L,), dtype=torch.int64, device=device)
+        self.kept_idx = torch.arange(n, dtype=torch.int32, device=device).expand(b, n).contiguous()
+        self.kept_count = torch.full((b,), n, dtype=torch.int32, device=device)
+        self.launches = 0
+
+    def _slice(self, t: torch.Tensor) -> torch.Tensor:
+        return t if self.hl == t.shape[1] else t[:, self.lh0:self.lh1].contiguous()
+
+    def compress_algo_bytes(self) -> int:
+        """Algorithmic bytes of this rank's compress launch: read 2*d bytes per kept K and V
+        row, write packed codes + fp16 scale per row, read the kept index per (row, head) once."""
+        b, d = self.cfg.batch, self.cfg.head_dim
+        dp = K.next_pow2(d)
+        pk, pv = K.packed_bytes(dp, self.levels[0]), K.packed_bytes(dp, self.levels[1])
+        return len(self.quant) * b * self.hl * self.cap * (2 * d * 2 + pk + pv + 4)
+
+    def importance(self, k_scored=None):
+        """Importance [b, T] on every rank: key-key over the scored block of layer 0 (per-head
+        column sums all-gathered), or the real scorer over this rank's layers/heads (sums
+        all-reduced).  k_scored: the block of layer-0 keys to score (default the resident one)."""
+        cfg = self.cfg
+        b, h, T = cfg.batch, cfg.heads, cfg.seq
+        if self.real:
+            acc = torch.zeros((b, T), dtype=torch.float32, device=self.dev)
+            for l in self.owned:
+                K.score_attention(self.Q[l], self.K[l], T - self.Q[l].shape[2], out=acc, accumulate=True)
+                self.launches += 3
+            # score_attention averages over the call's query heads: weight this rank's share
+            acc *= self.Q[self.owned[0]].shape[1] / (cfg.q_heads or h) if self.owned else 0.0
+            if self.world > 1:
+                dist.all_reduce(acc, group=self.group)
+            return acc / cfg.n_layers
+        k0 = self.K0 if k_scored is None else k_scored
+        if self.h1 > self.h0:
+            ph = K.score_keykey(k0, 32, per_head=True)
+            self.launches += 3
+        else:
+            ph = torch.zeros((b, 0, T), dtype=torch.float32, device=self.dev)
+        allh = S.gather_head_scores(ph, self.plan, self.group, self.gathered)
+        self.launches += 1
+        return K.reduce_heads(allh, float(h))
+
+    def step(self):
+        cfg = self.cfg
+        # global index of the compressed cache: the per-layer byte sizes of fixed-capacity
+        # outputs are known up front, so their exchange overlaps scoring and compression
+        _, sizes_work = S.gather_layer_index(self.sizes, self.plan, self.group, self.sizes_all, async_op=True)
+        if cfg.eviction_rate > 0:
+            imp = self.importance()
+            idx, cnt = K.select_keep(imp, cfg.sliding_window, self.nk)
+            self.launches += 1
+            self.kept_idx, self.kept_count = idx[:, :self.cap], cnt
+        if self.quant:
+            K.compress_layers([self.K[l] for l in self.quant], [self.V[l] for l in self.quant],
+                              key_levels=self.levels[0], value_levels=self.levels[1], kept_idx=self.kept_idx,
+                              kept_count=self.kept_count, n_kept=self.cap, rope_base=cfg.rope_base,
+                              rope_rows=cfg.seq, codes_out=self.codes)
+            self.launches += 2 * math.ceil(len(self.quant) / 96)  # key and value kernels
+        for l in self.prot:
+            K.gather_rows(self.K[l], self.kept_idx, self.cap, self.kept_count, out=self.prot_out[l][0])
+            K.gather_rows(self.V[l], self.kept_idx, self.cap, self.kept_count, out=self.prot_out[l][1])
+            self.launches += 2
+        if sizes_work is not None:
+            sizes_work.wait()
+
+    def compress_only(self):
+        K.compress_layers([self.K[l] for l in self.quant], [self.V[l] for l in self.quant],
+                          key_levels=self.levels[0], value_levels=self.levels[1], kept_idx=self.kept_idx,
+                          kept_count=self.kept_count, n_kept=self.cap, rope_base=self.cfg.rope_base,
+                          rope_rows=self.cfg.seq, codes_out=self.codes)
+
+    def dequant(self, outs):
+        return K.decompress_layers(self.codes, self.kept_idx, head_dim=self.cfg.head_dim, count=self.kept_count,
+                                   rope_base=self.cfg.rope_base, rope_rows=self.cfg.seq, out_k=outs[0],
+                                   out_v=outs[1])
+
+    def free(self):
+        self.K.clear()
+        self.V.clear()
+        self.Q.clear()
+        self.K0 = None
+
+
+def kernel_rooflines(sh: Shard, steps: int, peak: float) -> dict:
+    """Kernel-only compress and dequantize of the shard's quantized layers (CUDA events on the
+    launching stream, inputs far larger than L2)."""
+    if not sh.quant:
+        return {}
+    kms = timed(sh.compress_only, steps, 2, 1) / steps
+    cfg = sh.cfg
+    outs = ([torch.empty((cfg.batch, sh.hl, sh.cap, cfg.head_dim), dtype=torch.float16, device=sh.dev)
+             for _ in sh.quant],
+            [torch.empty((cfg.batch, sh.hl, sh.cap, cfg.head_dim), dtype=torch.float16, device=sh.dev)
+             for _ in sh.quant])
+    dms = timed(lambda: sh.dequant(outs), steps, 2, 1) / steps
+    del outs
+    algo = sh.compress_algo_bytes()
+    c = algo / (kms / 1e3) / 1e9
+    dq = algo / (dms / 1e3) / 1e9
+    return {"compress": {"achieved": round(c, 1), "frac": round(c / peak, 4), "launch_ms": round(kms, 4),
+                         "algo_bytes": algo},
+            "dequant": {"achieved": round(dq, 1), "frac": round(dq / peak, 4), "launch_ms": round(dms, 4),
+                        "algo_bytes": algo}}
+
+
+def per_config_rooflines(skip: int, dev, steps: int, peak: float) -> dict:
+    """Kernel-only compress / dequantize rooflines of configs 1-3 at their own shapes on this GPU
+    (one full cache each, keep set from the configuration's scorer)."""
+    out = {}
+    for cid in (1, 2, 3):
+        if cid == skip:
+            continue
+        cfg = syn.CONFIGS[cid]
+        sh = Shard(cfg, 0, 1, dev)
+        sh.step()
+        torch.cuda.synchronize()
+        r = kernel_rooflines(sh, max(5, min(steps, 20)), peak)
+        r["config"] = {"workload": cfg.name, "layers": cfg.n_layers, "batch": cfg.batch, "heads": cfg.heads,
+                       "seq": cfg.seq, "head_dim": cfg.head_dim, "kept_tokens": sh.cap}
+        out[f"config{cid}"] = r
+        sh.free()
+        del sh
+        torch.cuda.empty_cache()
+    return out
 
 
 # --------------------------------------------------------------------- CPU leg
@@ -270,96 +386,96 @@ def cpu_sample(cfg, seconds_hint: float = 15.0):
 
 
 # ------------------------------------------------------------------------ e2e
-def e2e_leg(sh: Shard, steps: int, group_layers: int = 8):
-    """End to end through the public API with the cache in pinned host memory.  Per step:
-    layer 0's keys of this rank's heads are copied host->device for scoring; the keep set is
-    selected on the device; for each group of layers a gather kernel reads only the kept rows
-    from host memory (mapped, over PCIe) into device memory and the compress kernel encodes
-    them there, and each group's codes and scales are copied device->host on a second stream
-    while the next group is read; protected layers' kept rows are gathered the same way."""
+class _Cache:
+    def __init__(self, ks, vs):
+        self.key_cache, self.value_cache = list(ks), list(vs)
+
+
+def e2e_leg(sh: Shard, steps: int):
+    """End to end through the drop-in API: NexusQuantEvict(layout="compressed", device=...,
+    result_on_host=True).compress(cache) on this rank's share of the cache held in pinned host
+    memory.  Per step: the scored keys cross PCIe to the device (on one GPU the API copies
+    layer 0's keys itself; with several ranks each copies its scored block and the importance,
+    sharded as in the device step, is handed to compress()), only the kept rows of every layer
+    cross PCIe (gather kernel), and the compressed cache comes back to pinned host memory group
+    by group while the next group is processed."""
     cfg = sh.cfg
     dev = sh.dev
+    if sh.real:
+        return None, "the real scorer needs the model's queries; e2e is measured on the key-key configs"
     try:
         host = {l: (torch.empty(sh.K[l].shape, dtype=sh.K[l].dtype, pin_memory=True),
                     torch.empty(sh.V[l].shape, dtype=sh.V[l].dtype, pin_memory=True)) for l in sh.owned}
-        host_k0 = host[0][0] if 0 in host else torch.empty(sh.K0.shape, dtype=sh.K0.dtype, pin_memory=True)
     except RuntimeError as e:
         return None, f"pinned host allocation failed: {e}"
     for l in sh.owned:
         host[l][0].copy_(sh.K[l])
         host[l][1].copy_(sh.V[l])
-    if 0 not in host:
-        host_k0.copy_(sh.K0)
     torch.cuda.synchronize()
+    single = sh.world == 1
+    k0_host = None
+    if not single and sh.K0 is not None:
+        k0_host = torch.empty(sh.K0.shape, dtype=sh.K0.dtype, pin_memory=True)
+        k0_host.copy_(sh.K0)
     # the device copies of the rank's layers are not used by this leg: free them
-    k0_dev = torch.empty_like(sh.K0)
-    for l in sh.owned:
-        sh.K[l] = sh.V[l] = None
+    sh.free()
     torch.cuda.empty_cache()
-    out_host = [(torch.empty(c.k_codes.shape, dtype=torch.uint8, pin_memory=True),
-                 torch.empty(c.v_codes.shape, dtype=torch.uint8, pin_memory=True),
-                 torch.empty(c.k_scales.shape, dtype=torch.float16, pin_memory=True),
-                 torch.empty(c.v_scales.shape, dtype=torch.float16, pin_memory=True)) for c in sh.codes]
-    prot_host = {l: (torch.empty(sh.prot_out[l][0].shape, dtype=torch.float16, pin_memory=True),
-                     torch.empty(sh.prot_out[l][1].shape, dtype=torch.float16, pin_memory=True))
-                 for l in sh.prot}
-    dn = torch.cuda.Stream(dev)
-    comp = torch.cuda.current_stream(dev)
-    b, h, T, d = cfg.batch, cfg.heads, cfg.seq, cfg.head_dim
+    cache = _Cache([host[l][0] for l in sh.owned], [host[l][1] for l in sh.owned])
+    prot_local = {i for i, l in enumerate(sh.owned) if l in sh.protected}
+    ev = NexusQuantEvict(bits=cfg.key_bits, key_bits=cfg.key_bits, value_bits=cfg.value_bits,
+                         eviction_rate=cfg.eviction_rate, sliding_window=cfg.sliding_window, obs_window=32,
+                         rope_base=cfg.rope_base, protect_boundary=0, protected_layers=prot_local,
+                         layout="compressed", device=dev, result_on_host=True, group_layers=8)
+    k0_dev = None if k0_host is None else torch.empty(k0_host.shape, dtype=k0_host.dtype, device=dev)
+    b, T, d = cfg.batch, cfg.seq, cfg.head_dim
     row = d * 2  # fp16 row bytes
-    # bytes that cross PCIe per step: layer 0's scored heads, every layer's kept rows; back: codes
-    h2d = b * (sh.h1 - sh.h0) * T * row + (len(sh.quant) + len(sh.prot)) * 2 * b * h * sh.cap * row
-    d2h = sum(sum(t.numel() * t.element_size() for t in o) for o in out_host)
-    d2h += sum(t.numel() * t.element_size() * 2 for t, _ in prot_host.values())
-    groups = [sh.quant[i:i + group_layers] for i in range(0, len(sh.quant), group_layers)]
+    scored = b * (sh.h1 - sh.h0) * T * row if (single or k0_host is not None) else 0
+    h2d = scored + len(sh.owned) * 2 * b * sh.hl * sh.cap * row
+    out = {}
 
     def step():
-        _, sizes_work = S.gather_layer_index(sh.sizes, sh.plan, sh.group, sh.sizes_all, async_op=True)
-        if sh.h1 > sh.h0:
-            k0_dev[:, sh.h0:sh.h1].copy_(host_k0[:, sh.h0:sh.h1], non_blocking=True)
-            ph = K.score_keykey(k0_dev, 32, head_range=(sh.h0, sh.h1), per_head=True)
+        if single:
+            res, _ = ev.compress(cache)
         else:
-            ph = torch.zeros((b, 0, T), dtype=torch.float32, device=dev)
-        allh = S.gather_head_scores(ph, sh.plan, sh.group, sh.gathered)
-        imp = K.reduce_heads(allh, float(h))
-        idx, cnt = K.select_keep(imp, cfg.sliding_window, sh.nk)
-        i0 = 0
-        for grp in groups:
-            K.compress_layers([host[l][0] for l in grp], [host[l][1] for l in grp], key_levels=sh.levels[0],
-                              value_levels=sh.levels[1], kept_idx=idx[:, :sh.cap], kept_count=cnt, n_kept=sh.cap,
-                              rope_base=cfg.rope_base, rope_rows=T, codes_out=sh.codes[i0:i0 + len(grp)],
-                              device=dev)
-            e = torch.cuda.Event()
-            e.record(comp)
-            dn.wait_event(e)
-            with torch.cuda.stream(dn):
-                for i in range(i0, i0 + len(grp)):
-                    c = sh.codes[i]
-                    for src, dst in zip((c.k_codes, c.v_codes, c.k_scales, c.v_scales), out_host[i]):
-                        dst.copy_(src, non_blocking=True)
-            i0 += len(grp)
-        for l in sh.prot:
-            K.gather_rows(host[l][0], idx[:, :sh.cap], sh.cap, cnt, out=sh.prot_out[l][0], device=dev)
-            K.gather_rows(host[l][1], idx[:, :sh.cap], sh.cap, cnt, out=sh.prot_out[l][1], device=dev)
-            e = torch.cuda.Event()
-            e.record(comp)
-            dn.wait_event(e)
-            with torch.cuda.stream(dn):
-                prot_host[l][0].copy_(sh.prot_out[l][0], non_blocking=True)
-                prot_host[l][1].copy_(sh.prot_out[l][1], non_blocking=True)
-        if sizes_work is not None:
-            sizes_work.wait()
-        done = torch.cuda.Event()
-        done.record(dn)
-        comp.wait_event(done)
+            if k0_dev is not None:
+                k0_dev.copy_(k0_host, non_blocking=True)
+            imp = sh.importance(k0_dev)
+            res, _ = ev.compress(cache, importance=imp)
+        out["res"] = res
 
     step()
     torch.cuda.synchronize()
+    res = out["res"]
+    d2h = res.nbytes() + res.kept_count.numel() * 4
     ms = timed(step, steps, 1, sh.world, sh.group)
-    return {"value": round(cfg.fp16_bytes * steps / (ms / 1e3) / 1e9, 3), "unit": "GB/s",
-            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": steps,
-            "ms_per_step": round(ms / steps, 3),
-            "path": "cache in pinned host memory; a gather kernel reads the kept rows across PCIe, then compress"}, None
+    e2e = {"value": round(cfg.fp16_bytes * steps / (ms / 1e3) / 1e9, 3), "unit": "GB/s",
+           "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": steps,
+           "ms_per_step": round(ms / steps, 3),
+           "path": "NexusQuantEvict(layout='compressed', device=cuda, result_on_host=True).compress(cache) on a "
+                   "cache in pinned host memory; kept rows gathered over PCIe, codes copied back per 8 layers"}
+    return (e2e, res), None
+
+
+def entropy_leg(cache, cfg, max_tokens: int = 2048) -> dict:
+    """zstd (level 22, system libzstd) of the temporal-delta streams of one quantized layer's first
+    ``max_tokens`` kept tokens: the reference's reported host post-step, outside every timed region."""
+    q = [i for i, l in enumerate(cache.layers) if not l.protected]
+    if not q:
+        return {"error": "no quantized layer"}
+    r = E.entropy_report(cache, level=22, layers=[q[0]], max_tokens=max_tokens, threads=os.cpu_count() or 1)
+    n_sym_total = sum(2 * cache.batch * l.codes.k_codes.shape[1] * cache.n_kept * cache.head_dim_padded
+                      for l in cache.layers if not l.protected)
+    idx_bytes = r["bits_per_symbol"] / 8.0 * n_sym_total
+    other = sum(l.nbytes() - (l.codes.k_codes.numel() + l.codes.v_codes.numel() if not l.protected else 0)
+                for l in cache.layers) + 24
+    total = idx_bytes + other
+    r.update({"sample": f"layer {q[0]} K+V, first {max_tokens} kept tokens of every head",
+              "packed_bits_per_symbol": round(8.0 * sum(l.codes.k_codes.numel() + l.codes.v_codes.numel()
+                                                        for l in cache.layers if not l.protected) / n_sym_total, 3),
+              "cache_ratio_vs_fp16_extrapolated": round(cfg.fp16_bytes / total, 3),
+              "bits_per_symbol": round(r["bits_per_symbol"], 4), "delta_seconds": round(r["delta_seconds"], 3),
+              "host_seconds": round(r["host_seconds"], 3)})
+    return r
 
 
 # ------------------------------------------------------------------- reference
@@ -375,10 +491,9 @@ def run_reference(args, cfg, rank, world):
     line = {"metric": METRIC, "impl": "reference", "value": round(v, 4), "unit": "GB/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": cfg.name, "layers": cfg.n_layers, "batch": cfg.batch, "heads": cfg.heads,
-                       "seq": cfg.seq, "head_dim": cfg.head_dim},
+            "config": config_dict(cfg, cap_for(cfg), world),
             "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": threads, "kind": "port",
-                             "sample": desc},
+                             "cpu": cpu_model(), "sample": desc},
             "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -414,7 +529,7 @@ def run_kernel(args, cfg, dev):
             return K.attend_compressed(q, lc, kidx, count=cnt, rope_base=cfg.rope_base, rope_rows=T)
 
         def unfused():
-            ok, ov = K.decompress_layers([lc], kidx, head_dim=d, count=cnt, rope_base=cfg.rope_base)
+            ok, ov = K.decompress_layers([lc], kidx, head_dim=d, count=cnt, rope_base=cfg.rope_base, rope_rows=T)
             kk = ok[0][0].float().repeat_interleave(8, 0)
             vv = ov[0][0].float().repeat_interleave(8, 0)
             w = torch.softmax(torch.einsum("hd,hnd->hn", q[0].float(), kk) * d ** -0.5, -1)
@@ -469,6 +584,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-per-config", action="store_true", help="skip the configs 1-3 kernel rooflines")
+    ap.add_argument("--no-entropy", action="store_true", help="skip the zstd post-step report")
     ap.add_argument("--profile", action="store_true", help="a few steps only (for ncu launch lists)")
     ap.add_argument("--kernel", choices=["attend", "merge"], default=None,
                     help="time one compressed-cache kernel instead of the headline step (1 GPU)")
@@ -497,7 +614,8 @@ def main():
         return
     group = None
     if world > 1:
-        dist.init_process_group("nccl", device_id=dev)
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
     sh = Shard(cfg, rank, world, dev, group)
     torch.cuda.synchronize()
 
@@ -509,18 +627,10 @@ def main():
         ms = timed(sh.step, args.steps, args.warmup, world, group)
     launches = sh.launches * args.steps // (args.steps + args.warmup)
 
-    # kernel-only: the compress launch on its stream, and the dequantize launch
-    kms = timed(sh.compress_only, args.steps, 2, 1) / args.steps
-    outs = ([torch.empty((cfg.batch, cfg.heads, sh.cap, cfg.head_dim), dtype=torch.float16, device=dev)
-             for _ in sh.quant],
-            [torch.empty((cfg.batch, cfg.heads, sh.cap, cfg.head_dim), dtype=torch.float16, device=dev)
-             for _ in sh.quant])
-    dms = timed(lambda: sh.dequant(outs), args.steps, 2, 1) / args.steps if sh.quant else float("nan")
     peak, peak_kind = peaks()
+    kr = kernel_rooflines(sh, args.steps, peak)
+    kms = kr["compress"]["launch_ms"] if kr else float("nan")
     algo = sh.compress_algo_bytes()
-    achieved = algo / (kms / 1e3) / 1e9 if sh.quant else 0.0
-    dq_bytes = algo  # dequantize moves the same bytes in the other direction
-    dq_achieved = dq_bytes / (dms / 1e3) / 1e9 if sh.quant else 0.0
     # DRAM bytes (read + write) per algorithmic byte of the compress kernel, from one ncu capture
     # (profiles/traffic.json); traffic of this launch = that ratio x this launch's algorithmic bytes.
     traffic = None
@@ -531,13 +641,27 @@ def main():
     except (OSError, KeyError, ValueError):
         pass
 
-    e2e, e2e_err = (None, "disabled")
+    e2e, e2e_err, host_cache = None, "disabled", None
     if not args.no_e2e and not args.profile:
-        e2e, e2e_err = e2e_leg(sh, args.e2e_steps)
+        got, e2e_err = e2e_leg(sh, args.e2e_steps)
+        if got is not None:
+            e2e, host_cache = got
+    sh.free()
+    torch.cuda.empty_cache()
+    ent = None
+    if rank == 0 and host_cache is not None and not args.no_entropy:
+        try:
+            ent = entropy_leg(host_cache, cfg)
+        except Exception as ex:  # reported, never fatal: it is outside the measured path
+            ent = {"error": f"{type(ex).__name__}: {ex}"}
+    per_cfg = None
+    if rank == 0 and world == 1 and not args.no_per_config and not args.profile:
+        per_cfg = per_config_rooflines(args.config, dev, args.steps, peak)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu and not args.profile:
         gbs, threads, desc = cpu_sample(cfg)
-        cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port", "sample": desc}
+        cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port", "cpu": cpu_model(),
+               "sample": desc}
 
     value = cfg.fp16_bytes * args.steps / (ms / 1e3) / 1e9
     if rank == 0:
@@ -545,18 +669,17 @@ def main():
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": cfg.name, "layers": cfg.n_layers, "batch": cfg.batch, "heads": cfg.heads,
-                       "seq": cfg.seq, "head_dim": cfg.head_dim, "key_bits": cfg.key_bits,
-                       "value_bits": cfg.value_bits, "eviction_rate": cfg.eviction_rate,
-                       "kept_tokens": sh.cap, "protected_layers": sorted(sh.protected),
-                       "parallelism": f"layer-sharded x{world}", "l2": f"inputs ({cfg.fp16_bytes / 1e9:.2f} GB) larger than L2; no flush"},
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "frac_of_spec_8tbs": round(achieved / 8000.0, 4),
-                         "traffic": traffic, "peak_kind": peak_kind,
-                         "kernel": "compress_kernel", "launch_ms": round(kms, 4), "algo_bytes": algo},
-            "dequant": {"value": round(dq_achieved, 1), "unit": "GB/s", "frac": round(dq_achieved / peak, 4),
-                        "frac_of_spec_8tbs": round(dq_achieved / 8000.0, 4),
-                        "launch_ms": round(dms, 4), "algo_bytes": dq_bytes},
+            "config": config_dict(cfg, sh.cap, world),
+            "roofline": {"bound": "hbm", "achieved": kr["compress"]["achieved"] if kr else 0.0, "peak": peak,
+                         "unit": "GB/s", "frac": kr["compress"]["frac"] if kr else 0.0,
+                         "frac_of_spec_8tbs": round((kr["compress"]["achieved"] if kr else 0.0) / 8000.0, 4),
+                         "traffic": traffic, "peak_kind": peak_kind, "kernel": "compress_kernel",
+                         "launch_ms": round(kms, 4), "algo_bytes": algo, "units": "rank 0's share"},
+            "dequant": ({"value": kr["dequant"]["achieved"], "unit": "GB/s", "frac": kr["dequant"]["frac"],
+                         "frac_of_spec_8tbs": round(kr["dequant"]["achieved"] / 8000.0, 4),
+                         "launch_ms": kr["dequant"]["launch_ms"], "algo_bytes": algo} if kr else None),
+            "per_config": per_cfg,
+            "entropy": ent,
             "cpu_baseline": cpu,
             "e2e": e2e if e2e is not None else {"value": None, "unit": "GB/s", "error": e2e_err},
             "gpu_launches": launches,

@@ -192,7 +192,10 @@ def delta_streams(cache, layers=None, max_tokens: Optional[int] = None) -> np.nd
                 m = min(cnt[bi], n) if max_tokens is None else min(cnt[bi], n, max_tokens)
                 if m <= 0:
                     continue
-                d = K.delta_codes(packed[bi, :, :m], cache.head_dim_padded, lev)  # [h, m, d_p]
+                src = packed[bi, :, :m]
+                if not src.is_cuda:  # a host-resident cache: the slice goes to the device for the delta
+                    src = src.to(torch.device("cuda", torch.cuda.current_device()))
+                d = K.delta_codes(src, cache.head_dim_padded, lev)  # [h, m, d_p]
                 parts.append(d.cpu().numpy().reshape(-1))
     return np.concatenate(parts) if parts else np.zeros((0,), np.int8)
 

@@ -278,8 +278,10 @@ def decompress_layers(codes: Sequence[LayerCodes], positions: torch.Tensor, *, h
                       count: Optional[torch.Tensor] = None, rope_base: float = 10000.0,
                       rope_scaling: Optional[dict] = None, key_sharpen: float = 1.0,
                       out_k: Optional[Sequence[torch.Tensor]] = None,
-                      out_v: Optional[Sequence[torch.Tensor]] = None):
-    """Dequantize layers to fp16 [b, h, n, head_dim]; keys re-encoded at `positions` [b, n]."""
+                      out_v: Optional[Sequence[torch.Tensor]] = None, rope_rows: Optional[int] = None):
+    """Dequantize layers to fp16 [b, h, n, head_dim]; keys re-encoded at `positions` [b, n].
+    rope_rows: RoPE table rows to use when every position is known to be below it; None reads
+    positions.max() (a host synchronisation) to size the table."""
     L = len(codes)
     if L == 0:
         return [], []
@@ -291,7 +293,10 @@ def decompress_layers(codes: Sequence[LayerCodes], positions: torch.Tensor, *, h
     positions = positions.to(device=dev, dtype=torch.int32).contiguous()
     if count is not None:
         count = count.to(device=dev, dtype=torch.int32).contiguous()
-    rows = int(positions.max().item()) + 1 if positions.numel() else 1
+    if rope_rows is not None:
+        rows = int(rope_rows)
+    else:
+        rows = int(positions.max().item()) + 1 if positions.numel() else 1
     cos, sin = TABLES.get(dev, head_dim, rope_base, rows, rope_scaling)
     ok = list(out_k) if out_k is not None else [None] * L
     ov = list(out_v) if out_v is not None else [None] * L

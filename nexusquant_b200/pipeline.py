@@ -116,13 +116,28 @@ def compress_cache_layers(keys: Sequence[torch.Tensor], values: Sequence[torch.T
                           kept_idx: Optional[torch.Tensor] = None, kept_count: Optional[torch.Tensor] = None,
                           n_kept: Optional[int] = None, protected: Sequence[int] = (),
                           rope_base: float = 10000.0, rope_scaling: Optional[dict] = None,
-                          position_offset: int = 0, mask: Optional[torch.Tensor] = None) -> CompressedKVCache:
+                          position_offset: int = 0, mask: Optional[torch.Tensor] = None,
+                          device: Optional[Union[int, str, torch.device]] = None, result_on_host: bool = False,
+                          out: Optional[CompressedKVCache] = None, group_layers: int = 8) -> CompressedKVCache:
     """Compress a whole cache to the compressed layout: quantized layers in one launch per
-    shape group, protected layers gathered to fp16."""
+    shape group, protected layers gathered to fp16.
+
+    The layers may sit in pinned host memory (pass ``device=``, default the current CUDA
+    device): only the kept rows then cross PCIe.  With ``result_on_host`` the compressed cache
+    is returned in pinned host memory, layer group by layer group (``group_layers`` layers
+    each), the copy of one group overlapping the gather and compression of the next; ``out``
+    (a cache this function returned before, same shapes) is written into instead of
+    allocating new host buffers."""
     L = len(keys)
     k0 = keys[0]
     b, h, seq, d = k0.shape
-    dev = k0.device
+    host_in = not k0.is_cuda
+    if host_in:
+        dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        if dev.type == "cuda" and dev.index is None:
+            dev = torch.device("cuda", torch.cuda.current_device())
+    else:
+        dev = k0.device
     if kept_idx is None:
         n_kept = seq if n_kept is None else n_kept
         kept_idx = torch.arange(n_kept, dtype=torch.int32, device=dev).expand(b, n_kept).contiguous()
@@ -131,26 +146,112 @@ def compress_cache_layers(keys: Sequence[torch.Tensor], values: Sequence[torch.T
     else:
         n_kept = kept_idx.shape[1] if n_kept is None else n_kept
         kept_idx = kept_idx[:, :n_kept].contiguous()
+    if kept_count is None:
+        kept_count = torch.full((b,), n_kept, dtype=torch.int32, device=dev)
     positions = kept_idx if position_offset == 0 else (kept_idx + position_offset)
     klv = K._levels_list(key_levels, L)
     vlv = K._levels_list(value_levels, L)
     prot = set(protected)
-    layers: List[Optional[CompressedLayer]] = [None] * L
     quant = [i for i in range(L) if i not in prot]
+    if result_on_host:
+        return _compress_to_host(keys, values, quant, sorted(i for i in prot if i < L), klv, vlv, kept_idx,
+                                 kept_count, n_kept, positions, rope_base, rope_scaling, mask, dev, group_layers, out)
+    layers: List[Optional[CompressedLayer]] = [None] * L
     for grp in _group_layers(keys, quant):
         codes = K.compress_layers([keys[i] for i in grp], [values[i] for i in grp],
                                   key_levels=[klv[i] for i in grp], value_levels=[vlv[i] for i in grp],
                                   kept_idx=kept_idx, kept_count=kept_count, positions=positions,
-                                  rope_base=rope_base, rope_scaling=rope_scaling)
+                                  rope_base=rope_base, rope_scaling=rope_scaling, device=dev if host_in else None)
         for i, c in zip(grp, codes):
             layers[i] = CompressedLayer(codes=c)
     for i in sorted(prot):
         if i >= L:
             continue
-        layers[i] = CompressedLayer(k_fp16=K.gather_rows(keys[i], kept_idx, n_kept, kept_count),
-                                    v_fp16=K.gather_rows(values[i], kept_idx, n_kept, kept_count))
+        layers[i] = CompressedLayer(
+            k_fp16=K.gather_rows(keys[i], kept_idx, n_kept, kept_count, device=dev if host_in else None),
+            v_fp16=K.gather_rows(values[i], kept_idx, n_kept, kept_count, device=dev if host_in else None))
     return CompressedKVCache(layers, positions.to(torch.int32), kept_count, seq, b, h, d, rope_base=rope_base,
                              rope_scaling=rope_scaling, mask=mask)
+
+
+_COPY_STREAMS = {}
+
+
+def _copy_stream(dev: torch.device) -> torch.cuda.Stream:
+    s = _COPY_STREAMS.get(str(dev))
+    if s is None:
+        s = _COPY_STREAMS[str(dev)] = torch.cuda.Stream(dev)
+    return s
+
+
+def _pinned_like(t: torch.Tensor) -> torch.Tensor:
+    return torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+
+
+def _compress_to_host(keys, values, quant, prot, klv, vlv, kept_idx, kept_count, n_kept, positions, rope_base,
+                      rope_scaling, mask, dev, group_layers, out) -> CompressedKVCache:
+    """compress_cache_layers(result_on_host=True): per group of layers, gather + compress on the
+    current stream, then copy the group's codes to pinned host memory on a second stream while
+    the next group is processed.  Device buffers of a group are released to the caching
+    allocator only after their copy (record_stream)."""
+    L = len(keys)
+    b, h, seq, d = keys[0].shape
+    comp = torch.cuda.current_stream(dev)
+    cp = _copy_stream(dev)
+    host_in = not keys[0].is_cuda
+    layers: List[Optional[CompressedLayer]] = [None] * L if out is None else list(out.layers)
+
+    def to_host(src: torch.Tensor, dst: Optional[torch.Tensor]) -> torch.Tensor:
+        if dst is None:
+            dst = _pinned_like(src)
+        elif dst.shape != src.shape or dst.dtype != src.dtype:
+            raise ValueError("out= does not match the shapes of this cache")
+        dst.copy_(src, non_blocking=True)
+        src.record_stream(cp)
+        return dst
+
+    def flush(done: List[int], made: dict):
+        ev = torch.cuda.Event()
+        ev.record(comp)
+        cp.wait_event(ev)
+        with torch.cuda.stream(cp):
+            for i in done:
+                prev = layers[i]
+                if i in made and isinstance(made[i], K.LayerCodes):
+                    c = made[i]
+                    pc = prev.codes if prev is not None and not prev.protected else None
+                    layers[i] = CompressedLayer(codes=K.LayerCodes(
+                        to_host(c.k_codes, pc.k_codes if pc else None), to_host(c.v_codes, pc.v_codes if pc else None),
+                        to_host(c.k_scales, pc.k_scales if pc else None),
+                        to_host(c.v_scales, pc.v_scales if pc else None), c.key_levels, c.value_levels))
+                else:
+                    kf, vf = made[i]
+                    pk_ = prev.k_fp16 if prev is not None and prev.protected else None
+                    pv_ = prev.v_fp16 if prev is not None and prev.protected else None
+                    layers[i] = CompressedLayer(k_fp16=to_host(kf, pk_), v_fp16=to_host(vf, pv_))
+
+    groups = [quant[i:i + group_layers] for i in range(0, len(quant), max(1, group_layers))]
+    for grp in groups:
+        for sub in _group_layers(keys, grp):
+            codes = K.compress_layers([keys[i] for i in sub], [values[i] for i in sub],
+                                      key_levels=[klv[i] for i in sub], value_levels=[vlv[i] for i in sub],
+                                      kept_idx=kept_idx, kept_count=kept_count, positions=positions,
+                                      rope_base=rope_base, rope_scaling=rope_scaling,
+                                      device=dev if host_in else None)
+            flush(sub, dict(zip(sub, codes)))
+    for i in prot:
+        kf = K.gather_rows(keys[i], kept_idx, n_kept, kept_count, device=dev if host_in else None)
+        vf = K.gather_rows(values[i], kept_idx, n_kept, kept_count, device=dev if host_in else None)
+        flush([i], {i: (kf, vf)})
+    done = torch.cuda.Event()
+    done.record(cp)
+    comp.wait_event(done)  # the caller's stream (and a synchronize on it) covers the copies
+    pos_h = out.positions if out is not None else torch.empty((b, n_kept), dtype=torch.int32, pin_memory=True)
+    cnt_h = out.kept_count if out is not None else torch.empty((b,), dtype=torch.int32, pin_memory=True)
+    pos_h.copy_(positions.to(torch.int32), non_blocking=True)
+    cnt_h.copy_(kept_count.to(torch.int32), non_blocking=True)
+    return CompressedKVCache(layers, pos_h, cnt_h, seq, b, h, d, rope_base=rope_base, rope_scaling=rope_scaling,
+                             mask=mask)
 
 
 # --------------------------------------------------------------------------- compressors
@@ -246,7 +347,8 @@ class NexusQuantEvict:
                  adaptive_context: bool = False, protected_positions: Optional[torch.Tensor] = None,
                  compress_layers: str = "all", layer_bit_profile: str = "uniform",
                  distance_graduated: bool = False, merge_eviction: bool = False,
-                 layout: str = "fake_quant", sharpen: bool = False):
+                 layout: str = "fake_quant", sharpen: bool = False, device=None, result_on_host: bool = False,
+                 group_layers: int = 8):
         if scorer not in ("key-key", "real"):
             raise ValueError(f"scorer must be 'key-key' or 'real', got {scorer!r}")
         if not (isinstance(eviction_rate, (int, float)) or eviction_rate == "auto"):
@@ -280,6 +382,12 @@ class NexusQuantEvict:
         self.merge_eviction = merge_eviction
         self.layout = layout
         self.sharpen = sharpen
+        # caches in pinned host memory: the device that compresses them, and whether the
+        # compressed cache comes back to pinned host memory (layout="compressed" only)
+        self.device = device
+        self.result_on_host = result_on_host
+        self.group_layers = group_layers
+        self._host_out: Optional[CompressedKVCache] = None
         self._swa_layer_indices = None
         self.last_compressed: Optional[CompressedKVCache] = None
 
@@ -288,6 +396,16 @@ class NexusQuantEvict:
         if self.compress_layers != "global_only":
             return
         self._swa_layer_indices = _swa_layers_from_config(model_config)
+
+    def _reusable_host_out(self, n_layers: int, b: int, cap: int) -> Optional[CompressedKVCache]:
+        """The previous host-resident result, written into again when the shapes agree (pinned host
+        allocation is slow); the caller must be done with it before compressing again."""
+        o = self._host_out
+        if not self.result_on_host or o is None:
+            return None
+        if len(o.layers) != n_layers or o.batch != b or o.n_kept != cap:
+            return None
+        return o
 
     def _find_scoring_layer(self, past_key_values, n_layers: int) -> int:
         """First global layer for hybrid models, else 0 (nexusquant/pipeline.py:726-738)."""
@@ -413,15 +531,35 @@ class NexusQuantEvict:
             return self._score_importance_real(model, input_ids)
         return self._score_importance(k_score)
 
+    def _compute_device(self, k_score: torch.Tensor) -> torch.device:
+        if k_score.is_cuda:
+            return k_score.device
+        if self.layout != "compressed":
+            raise ValueError("a cache in host memory needs layout='compressed' (the fake-quant layout writes "
+                             "fp16 tensors of the original shape back into the cache)")
+        if not k_score.is_pinned():
+            raise RuntimeError("a cache in host memory must be in pinned memory")
+        dev = torch.device(self.device) if self.device is not None else torch.device("cuda")
+        return torch.device("cuda", torch.cuda.current_device()) if dev.index is None else dev
+
     def compress(self, past_key_values, model=None, input_ids=None, importance: Optional[torch.Tensor] = None):
         """Evict + quantize.  Returns (past_key_values, prefix_attention_mask (b, seq) float) in the
-        fake-quant layout, or (CompressedKVCache, mask) with layout="compressed"."""
+        fake-quant layout, or (CompressedKVCache, mask) with layout="compressed".  With
+        layout="compressed" the cache may sit in pinned host memory: the scoring layer's keys are
+        copied to ``device``, only kept rows of the other layers cross PCIe, and with
+        ``result_on_host`` the compressed cache comes back in pinned host memory."""
         n_layers = _num_layers(past_key_values)
         score_layer = self._find_scoring_layer(past_key_values, n_layers)
         k_score, _ = _get_layer_kv(past_key_values, score_layer)
-        device = k_score.device
+        device = self._compute_device(k_score)
+        host_in = not k_score.is_cuda
         b, _, seq, _ = k_score.shape
+        if importance is None and host_in:
+            if self.scorer == "real":
+                raise ValueError("scorer='real' with a host-resident cache: pass importance=")
+            importance = self._score_importance(k_score.to(device, non_blocking=True))
         importance = self._importance(past_key_values, n_layers, model, input_ids, importance)
+        importance = importance.to(device)
         rate = self._resolve_rate(importance, seq)
         kept_idx, kept_count, cap = self._keep_set(importance, seq, rate)
         mask = _mask_from_kept(kept_idx, kept_count, seq)
@@ -431,6 +569,8 @@ class NexusQuantEvict:
         levels = [self._resolve_layer_levels(l, n_layers) for l in range(n_layers)]
         ks, vs = zip(*[_get_layer_kv(past_key_values, l) for l in range(n_layers)])
         if self.merge_eviction and not self.soft_eviction:
+            if host_in:
+                raise NotImplementedError("merge_eviction with a host-resident cache")
             # value merging before hard eviction (pipeline.py:1185-1187), on copies of the
             # full-length layers as the reference writes merged clones into the cache
             vs = [v.clone() if v.shape[2] == seq else v for v in vs]
@@ -441,7 +581,12 @@ class NexusQuantEvict:
             out = compress_cache_layers(list(ks), list(vs), key_levels=[lv[0] for lv in levels],
                                         value_levels=[lv[1] for lv in levels], kept_idx=kept_idx,
                                         kept_count=kept_count, n_kept=cap, protected=sorted(skip),
-                                        rope_base=self.rope_base, rope_scaling=self.rope_scaling, mask=mask)
+                                        rope_base=self.rope_base, rope_scaling=self.rope_scaling, mask=mask,
+                                        device=device, result_on_host=self.result_on_host,
+                                        out=self._reusable_host_out(n_layers, b, cap),
+                                        group_layers=self.group_layers)
+            if self.result_on_host:
+                self._host_out = out
             self.last_compressed = out
             return out, mask
         todo = [l for l in range(n_layers) if l not in skip]

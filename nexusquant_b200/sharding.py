@@ -1,7 +1,15 @@
-"""Layer-sharded compression across the GPUs of one node (one process per GPU).
+"""Sharded compression across the GPUs of one node (one process per GPU).
 
-Once the keep set is known every layer compresses independently, so ranks own
-whole layers.  The only cross-GPU traffic:
+Once the keep set is known every (layer, KV head) row block compresses
+independently.  Two plans:
+
+* ``heads`` (when the world size divides the KV heads): rank r owns KV heads
+  [r*h/N, (r+1)*h/N) of every layer -- the same slice it scores -- so every rank
+  moves exactly 1/N of the cache, protected layers included.
+* ``layers`` (otherwise): ranks own whole layers, balanced by cost
+  (longest-processing-time greedy).
+
+The only cross-GPU traffic:
 
 1. Keep set.  Under ``NexusQuantEvict.compress`` semantics layer 0's importance
    decides every layer (nexusquant/pipeline.py:1066-1098).  Each rank scores a
@@ -68,26 +76,44 @@ class ShardPlan:
     world: int
     n_layers: int
     heads: int
-    layers: Tuple[int, ...]       # all layers this rank owns
-    quantized: Tuple[int, ...]    # owned layers that are compressed
-    protected: Tuple[int, ...]    # owned layers kept at fp16
-    head_begin: int
+    layers: Tuple[int, ...]       # all layers this rank holds rows of
+    quantized: Tuple[int, ...]    # those that are compressed
+    protected: Tuple[int, ...]    # those kept at fp16
+    head_begin: int               # KV heads this rank scores
     head_end: int
     heads_per_rank: int
+    mode: str = "layers"          # "heads": [head_begin, head_end) of every layer; "layers": whole layers
 
     @property
     def scores_heads(self) -> bool:
         return self.head_end > self.head_begin
 
+    @property
+    def layer_heads(self) -> Tuple[int, int]:
+        """KV heads of each owned layer that this rank compresses."""
+        return (self.head_begin, self.head_end) if self.mode == "heads" else (0, self.heads)
 
-def make_plan(n_layers: int, heads: int, protect_boundary: int, rank: int, world: int) -> ShardPlan:
+
+def plan_mode(heads: int, world: int, mode: str = "auto") -> str:
+    if mode == "auto":
+        return "heads" if heads % world == 0 else "layers"
+    if mode not in ("heads", "layers"):
+        raise ValueError(f"mode must be 'auto', 'heads' or 'layers', got {mode!r}")
+    if mode == "heads" and heads % world:
+        raise ValueError(f"mode='heads' needs the world size ({world}) to divide the KV heads ({heads})")
+    return mode
+
+
+def make_plan(n_layers: int, heads: int, protect_boundary: int, rank: int, world: int,
+              mode: str = "auto") -> ShardPlan:
     if not 0 <= rank < world:
         raise ValueError(f"rank {rank} outside world {world}")
+    m = plan_mode(heads, world, mode)
     prot = protected_layers(n_layers, protect_boundary)
-    owned = assign_layers(n_layers, prot, world)[rank]
+    owned = list(range(n_layers)) if m == "heads" else assign_layers(n_layers, prot, world)[rank]
     h0, h1, per = head_block(heads, rank, world)
     return ShardPlan(rank, world, n_layers, heads, tuple(owned), tuple(l for l in owned if l not in prot),
-                     tuple(l for l in owned if l in prot), h0, h1, per)
+                     tuple(l for l in owned if l in prot), h0, h1, per, m)
 
 
 def gather_head_scores(per_head: torch.Tensor, plan: ShardPlan, group=None,
@@ -149,6 +175,22 @@ def layer_owners(assignment: Sequence[Sequence[int]], n_layers: int) -> List[int
     if -1 in owner:
         raise ValueError(f"layer {owner.index(-1)} has no owner")
     return owner
+
+
+def unit_table(sizes_all: torch.Tensor) -> List[Tuple[int, int, int, int]]:
+    """Global index for either plan: (layer, rank, byte offset, size) of every non-empty
+    (layer, rank) block, in layer-major then rank order -- the concatenation order of the
+    compressed cache (a layer's head slices follow each other in head order)."""
+    s = sizes_all.cpu()
+    world, n_layers = s.shape
+    out, off = [], 0
+    for l in range(n_layers):
+        for r in range(world):
+            n = int(s[r, l])
+            if n:
+                out.append((l, r, off, n))
+                off += n
+    return out
 
 
 def layer_table(sizes_all: torch.Tensor, owners: Sequence[int]) -> List[Tuple[int, int, int]]:

@@ -131,3 +131,13 @@ def device_layer(cfg: CacheConfig, layer: int, device, seed: int = DEFAULT_SEED,
         out_v.copy_(v)
         return out_k, out_v
     return k.to(cfg.dtype), v.to(cfg.dtype)
+
+
+def device_queries(cfg: CacheConfig, layer: int, device, seed: int = DEFAULT_SEED,
+                   n_queries: Optional[int] = None) -> torch.Tensor:
+    """Same distribution as cpu_queries, drawn on `device` (fast; not bit-identical)."""
+    b, hq, T = cfg.batch, cfg.q_heads or cfg.heads, cfg.seq
+    nq = n_queries or cfg.n_queries
+    g = torch.Generator(device=device).manual_seed(seed * 1000 + 500 + layer)
+    q = torch.randn(b, hq, nq, cfg.head_dim, generator=g, device=device)
+    return apply_rope(q, cfg.rope_base, offset=T - nq).to(cfg.dtype)

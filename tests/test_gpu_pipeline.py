@@ -154,3 +154,35 @@ def test_hf_hook_tiny_llama():
         hk = hooked.layers[l].keys
         assert hk.dtype == torch.float16 and hk.shape == (1, 2, 90, 64)
         assert int((hk.abs().sum(-1) != 0).sum(-1).max().item()) == n_kept
+
+
+def test_evict_host_cache_through_api_matches_device():
+    """NexusQuantEvict(layout="compressed") on a cache in pinned host memory, result copied back
+    to pinned host memory group by group, equals the device-resident call bit for bit; a second
+    call writes into the first call's host buffers."""
+    cfg = syn.CacheConfig("host", 6, 2, 4, 600, 128, key_bits=2, value_bits=2, eviction_rate=0.7)
+    ks, vs = zip(*[syn.cpu_layer(cfg, l) for l in range(6)])
+    ref, mask_d = nq.NexusQuantEvict(bits=2, eviction_rate=0.7, protect_boundary=1, layout="compressed").compress(
+        FakeCache([k.to(DEV) for k in ks], [v.to(DEV) for v in vs]))
+    host = FakeCache([k.pin_memory() for k in ks], [v.pin_memory() for v in vs])
+    ev = nq.NexusQuantEvict(bits=2, eviction_rate=0.7, protect_boundary=1, layout="compressed", device=DEV,
+                            result_on_host=True, group_layers=2)
+    first = None
+    for _ in range(2):
+        out, mask_h = ev.compress(host)
+        torch.cuda.synchronize()
+        assert torch.equal(mask_h.cpu(), mask_d.cpu())
+        assert torch.equal(out.positions, ref.positions.cpu()) and out.positions.is_pinned()
+        for lo, lr in zip(out.layers, ref.layers):
+            assert lo.protected == lr.protected
+            if lo.protected:
+                pairs = [(lo.k_fp16, lr.k_fp16), (lo.v_fp16, lr.v_fp16)]
+            else:
+                pairs = [(getattr(lo.codes, f), getattr(lr.codes, f)) for f in ("k_codes", "v_codes", "k_scales",
+                                                                                  "v_scales")]
+            for a, b in pairs:
+                assert not a.is_cuda and a.is_pinned() and torch.equal(a, b.cpu())
+        if first is None:
+            first = out.layers[2].codes.k_codes.data_ptr()
+        else:
+            assert out.layers[2].codes.k_codes.data_ptr() == first

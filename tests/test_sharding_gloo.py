@@ -46,12 +46,12 @@ def _per_head(K, h0, h1):
     return out
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, mode="layers"):
     try:
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
         dist.init_process_group("gloo", rank=rank, world_size=world)
         from oracle import oracle as orc
-        plan = S.make_plan(L, H, PB, rank, world)
+        plan = S.make_plan(L, H, PB, rank, world, mode=mode)
         K = _keys()
         ph = torch.from_numpy(_per_head(K, plan.head_begin, plan.head_end))
         allh = S.gather_head_scores(ph, plan)
@@ -73,14 +73,24 @@ def _worker(rank, world, port, q):
         if work is not None:
             work.wait()
         assert torch.equal(table_async, sizes_all)
-        owners = S.layer_owners(S.assign_layers(L, S.protected_layers(L, PB), world), L)
-        table = S.layer_table(sizes_all, owners)
         prot_set = S.protected_layers(L, PB)
-        off = 0
-        for l, (r, o, n) in enumerate(table):
-            assert o == off and n == (50000 + l if l in prot_set else 1000 + 7 * l)
-            assert l in S.make_plan(L, H, PB, r, world).layers
-            off += n
+        if mode == "layers":
+            owners = S.layer_owners(S.assign_layers(L, prot_set, world), L)
+            table = S.layer_table(sizes_all, owners)
+            off = 0
+            for l, (r, o, n) in enumerate(table):
+                assert o == off and n == (50000 + l if l in prot_set else 1000 + 7 * l)
+                assert l in S.make_plan(L, H, PB, r, world).layers
+                off += n
+        else:
+            # every rank holds its head slice of every layer: world blocks per layer
+            assert plan.layers == tuple(range(L)) and plan.layer_heads == (plan.head_begin, plan.head_end)
+            units = S.unit_table(sizes_all)
+            assert [(l, r) for l, r, _, _ in units] == [(l, r) for l in range(L) for r in range(world)]
+            off = 0
+            for l, r, o, n in units:
+                assert o == off and n == (50000 + l if l in prot_set else 1000 + 7 * l)
+                off += n
         q.put((rank, "ok", mask.sum()))
         dist.destroy_process_group()
     except Exception as e:  # report to the parent, which fails the test
@@ -88,12 +98,12 @@ def _worker(rank, world, port, q):
         raise
 
 
-@pytest.mark.parametrize("world", [2, 3])
-def test_sharded_keep_set_and_index_gloo(world):
+@pytest.mark.parametrize("world,mode", [(2, "layers"), (3, "layers"), (5, "heads")])
+def test_sharded_keep_set_and_index_gloo(world, mode):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, mode)) for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=180) for _ in range(world)]
@@ -124,6 +134,22 @@ def test_head_blocks_cover_heads(heads, world):
         assert 0 <= h0 <= h1 <= heads and h1 - h0 <= per
         seen += list(range(h0, h1))
     assert seen == list(range(heads))
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_head_plan_config4_is_even(world):
+    """Config 4 (80 layers, 8 KV heads): every rank compresses 8/world heads of all 76 quantized
+    layers and gathers the same slice of the 4 protected ones."""
+    plans = [S.make_plan(80, 8, 2, r, world) for r in range(world)]
+    assert all(p.mode == "heads" for p in plans)
+    assert [p.layer_heads for p in plans] == [(r * 8 // world, (r + 1) * 8 // world) for r in range(world)]
+    assert all(len(p.quantized) == 76 and len(p.protected) == 4 for p in plans)
+
+
+def test_plan_modes():
+    assert S.make_plan(80, 8, 2, 0, 3).mode == "layers"  # 3 does not divide 8
+    with pytest.raises(ValueError):
+        S.make_plan(80, 8, 2, 0, 3, mode="heads")
 
 
 def test_plan_rejects_bad_rank():
