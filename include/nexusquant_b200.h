@@ -115,7 +115,9 @@ typedef struct nq_compress_params {
                                     is the device pointer); the kernel then reads only the kept
                                     rows across PCIe.  Checked with cudaPointerGetAttributes:
                                     anything else returns NQ_ERR_INVALID_ARG. */
-  int32_t *error_flag;           /* optional device int32 (reserved; no bounded wait sets it) */
+  int32_t *error_flag;           /* optional device int32; unused: the compress kernels have no
+                                    device-side waits.  Expired waits of the scorer are reported
+                                    by nq_device_error(). */
   const nq_layer_io_t *layers;   /* HOST array [n_layers] */
   int32_t n_layers;
 } nq_compress_params_t;
@@ -336,6 +338,21 @@ nq_status_t nq_unpack_codes(const uint8_t *packed, int64_t rows, int32_t head_di
                             int8_t *codes, nq_stream_t stream);
 nq_status_t nq_pack_nibbles(const int8_t *codes, int64_t rows, int32_t d, uint8_t *packed, nq_stream_t stream);
 nq_status_t nq_unpack_nibbles(const uint8_t *packed, int64_t rows, int32_t d, int8_t *codes, nq_stream_t stream);
+
+/*
+ * Device-side failure reporting (no counterpart in the reference, which has no device code).
+ *
+ * Every device-side wait in this library (the tensor-core scorer's waits on TMA and MMA
+ * completion) has an iteration limit.  A wait that runs out makes its kernel stop early,
+ * release what it holds and OR a bit into a per-device error word; the scores it leaves are
+ * then not valid.  nq_device_error synchronizes `stream`, stores the word in *bits (if bits is
+ * not NULL), clears it, and returns NQ_ERR_TIMEOUT if any bit was set, else NQ_OK.
+ * Bits: 1 = scorer wait, 2 = nq_wait_selftest.
+ */
+nq_status_t nq_device_error(int32_t *bits, nq_stream_t stream);
+/* Test hook: one CTA waits on an mbarrier that nothing arrives on, for max_iters (1..2^20)
+ * tries, then records the expiry (bit 2) -- the failure path without any copy in flight. */
+nq_status_t nq_wait_selftest(uint32_t max_iters, nq_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -107,6 +107,8 @@ _PROTOS = {
     "nq_unpack_nibbles": (c_i32, [c_vp, c_i64, c_i32, c_vp, c_vp]),
     "nq_merge_apply": (c_i32, [ctypes.POINTER(c_vp), c_i32, c_i32, c_i32, c_i32, c_i32, c_i64, c_i64, c_vp, c_vp,
                                c_i32, c_vp, c_vp, c_vp]),
+    "nq_device_error": (c_i32, [ctypes.POINTER(c_i32), c_vp]),
+    "nq_wait_selftest": (c_i32, [ctypes.c_uint32, c_vp]),
 }
 
 EXPORTED = tuple(_PROTOS)

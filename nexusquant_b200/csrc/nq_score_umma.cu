@@ -23,6 +23,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include "../../include/nexusquant_b200.h"
 #include "nq_common.cuh"
 #include "nq_internal.h"
 
@@ -31,6 +32,11 @@ namespace nq {
 namespace {
 
 constexpr int kUmKeys = 128;     // keys per tile (MMA M)
+
+// Device error word of this library's bounded waits (one per device): bit 0 a scorer wait,
+// bit 1 the wait self-test.  Read and cleared by nq_device_error().
+__device__ unsigned int g_wait_error;
+constexpr unsigned int kWaitErrScore = 1u, kWaitErrSelfTest = 2u;
 constexpr int kUmStages = 3;     // key-tile stages
 constexpr float kLog2eU = 1.4426950408889634f;
 
@@ -309,10 +315,12 @@ __global__ void __launch_bounds__(UmLayout<D, NQP>::kThreads, 1)
       w.pl[o] = s;
     }
   }
-  // drain: the MMA issued for a tile that was not consumed must finish before TMEM is freed
+  // drain: the MMA issued for a tile that was not consumed must finish before TMEM is freed;
+  // the expired wait is recorded in the device error word (nq_device_error)
   if (threadIdx.x == 0 && err) {
     mbar_wait(&mbar[0], 0, 1u << 20);
     mbar_wait(&mbar[1], 0, 1u << 20);
+    atomicOr(&g_wait_error, kWaitErrScore);
   }
   tc_fence_before();
   __syncthreads();
@@ -453,4 +461,38 @@ cudaError_t launch_score_umma(const ScoreArgs& a, float* colsum, void* ws, cudaS
   return umma_nq<64>(a, colsum, ws, s);
 }
 
+// A bounded wait that is made to expire on purpose: one CTA waits on an mbarrier nothing
+// arrives on, with nothing else in flight, and records the expiry like a real kernel would.
+__global__ void wait_selftest_kernel(uint32_t max_iters) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && !mbar_wait(&bar, 0, max_iters)) atomicOr(&g_wait_error, kWaitErrSelfTest);
+}
+
 }  // namespace nq
+
+extern "C" nq_status_t nq_device_error(int32_t* bits, nq_stream_t stream) {
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  unsigned int v = 0;
+  if (cudaMemcpyFromSymbolAsync(&v, nq::g_wait_error, sizeof(v), 0, cudaMemcpyDeviceToHost, s) != cudaSuccess)
+    return NQ_ERR_CUDA;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return NQ_ERR_CUDA;
+  if (v) {
+    const unsigned int zero = 0;
+    if (cudaMemcpyToSymbolAsync(nq::g_wait_error, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess)
+      return NQ_ERR_CUDA;
+  }
+  if (bits) *bits = static_cast<int32_t>(v);
+  return v ? NQ_ERR_TIMEOUT : NQ_OK;
+}
+
+extern "C" nq_status_t nq_wait_selftest(uint32_t max_iters, nq_stream_t stream) {
+  if (max_iters == 0 || max_iters > (1u << 20)) return NQ_ERR_INVALID_ARG;
+  nq::wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(max_iters);
+  return cudaGetLastError() == cudaSuccess ? NQ_OK : NQ_ERR_CUDA;
+}

@@ -355,6 +355,18 @@ def score_keykey(k: torch.Tensor, obs_window: int = 32, head_range=None, per_hea
     return out
 
 
+def check_device_errors(device=None) -> int:
+    """Synchronize the device's current stream and raise NexusQuantError (NQ_ERR_TIMEOUT) if a
+    bounded device-side wait expired since the last check (the scorer's results are then not
+    valid); clears the device's error word.  Returns 0."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    bits = ctypes.c_int32(0)
+    with torch.cuda.device(dev):
+        st = N.load().nq_device_error(ctypes.byref(bits), _stream(dev))
+    N.check("nq_device_error", st)
+    return bits.value
+
+
 def reduce_heads(per_head: torch.Tensor, divisor: float, out: Optional[torch.Tensor] = None,
                  accumulate: bool = False) -> torch.Tensor:
     _require_cuda(per_head)

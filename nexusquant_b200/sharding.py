@@ -27,6 +27,7 @@ gloo for the CPU tests).
 from __future__ import annotations
 
 import math
+import time
 from dataclasses import dataclass
 from typing import Iterable, List, Optional, Sequence, Tuple
 
@@ -203,3 +204,46 @@ def layer_table(sizes_all: torch.Tensor, owners: Sequence[int]) -> List[Tuple[in
         table.append((r, off, n))
         off += n
     return table
+
+
+# ------------------------------------------------------------------ failure handling
+class RankFailure(RuntimeError):
+    """A peer rank did not reach a step in time, or sent an invalid message."""
+
+
+def step_checkpoint(store, rank: int, world: int, step: int, timeout: float = 30.0) -> None:
+    """Host heartbeat before a step's collectives.  Every rank posts ``step`` to the store and
+    waits (bounded) for all others, so a rank that left between steps is named before any
+    collective of the next step is launched -- the survivors raise RankFailure instead of
+    blocking in NCCL.  ``store`` is the process group's store (or any c10d Store)."""
+    key = "nq/step/{}/{}".format
+    store.set(key(step, rank), b"1")
+    deadline = time.monotonic() + timeout
+    missing = [r for r in range(world) if r != rank]
+    while missing:
+        missing = [r for r in missing if not store.check([key(step, r)])]
+        if not missing:
+            return
+        if time.monotonic() > deadline:
+            raise RankFailure(f"rank(s) {missing} did not reach step {step} within {timeout:g} s")
+        time.sleep(0.005)
+
+
+def validate_index(sizes_all: torch.Tensor, n_layers: int, heads: int, protect_boundary: int,
+                   expected=None) -> None:
+    """Check a gathered size table before using it: every rank's row must be non-negative and
+    non-zero exactly at the layers its plan holds, and equal ``expected(rank, layer)`` where that
+    is given (fixed-capacity outputs make the sizes known).  Raises RankFailure naming the rank."""
+    s = sizes_all.detach().cpu().reshape(-1, n_layers)
+    world = s.shape[0]
+    for r in range(world):
+        plan = make_plan(n_layers, heads, protect_boundary, r, world)
+        held = set(plan.layers)
+        for l in range(n_layers):
+            n = int(s[r, l])
+            if n < 0 or (n > 0) != (l in held):
+                raise RankFailure(f"rank {r} reported {n} bytes for layer {l}, which it "
+                                  f"{'holds' if l in held else 'does not hold'}")
+            if expected is not None and l in held and n != int(expected(r, l)):
+                raise RankFailure(f"rank {r} reported {n} bytes for layer {l}, expected {int(expected(r, l))}")
+
