@@ -419,17 +419,25 @@ cudaError_t run_umma(const ScoreArgs& a, float* colsum, void* ws, cudaStream_t s
   cudaError_t e;
   if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
   if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
-  // two CTAs per SM (shared memory), each walking a run of tiles of one head
-  const long long heads = (long long)a.batch * Hr;
-  int tpc = (int)((tiles * heads + 2LL * sms - 1) / (2LL * sms));
-  tpc = max(1, min(tpc, tiles));
-  const int chunks = (tiles + tpc - 1) / tpc;
-  const uint32_t idesc = f16_idesc(a.in_dtype, kUmKeys, NQP);
   auto k1 = score_umma<D, NQP, 1>;
   auto k3 = score_umma<D, NQP, 3>;
   const int smem = Lo::kBytes;
   if ((e = cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess) return e;
   if ((e = cudaFuncSetAttribute(k3, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess) return e;
+  // all of the unified L1/shared array as shared memory, so two CTAs fit per SM
+  if ((e = cudaFuncSetAttribute(k1, cudaFuncAttributePreferredSharedMemoryCarveout, 100)) != cudaSuccess) return e;
+  if ((e = cudaFuncSetAttribute(k3, cudaFuncAttributePreferredSharedMemoryCarveout, 100)) != cudaSuccess) return e;
+  // one wave: each (batch, head) row gets `chunks` CTAs walking equal runs of its tiles, with
+  // chunks x rows at most the resident CTA slots (more rows than slots: one CTA per row)
+  const long long rows = (long long)a.batch * Hr;
+  // resident CTAs per SM: two of the 32-query kernel, one of the 64-query kernel (registers);
+  // (measured: planning the 32-query kernel for two beats the occupancy query's answer of one)
+  const long long slots = (long long)sms * (NQP == 32 ? 2 : 1);
+  long long want = slots / (rows > 0 ? rows : 1);
+  want = want < 1 ? 1 : (want > tiles ? tiles : want);
+  const int tpc = (int)((tiles + want - 1) / want);
+  const int chunks = (tiles + tpc - 1) / tpc;
+  const uint32_t idesc = f16_idesc(a.in_dtype, kUmKeys, NQP);
   const dim3 g(chunks, Hr, a.batch);
   k1<<<g, Lo::kThreads, smem, s>>>(kmap, qmap, a, w, colsum, tpc, idesc);
   score_umma_combine<<<dim3(a.n_q, Hr, a.batch), 32, 0, s>>>(a, w, chunks);
