@@ -429,7 +429,15 @@ class NexusQuantEvict:
         return K.score_keykey(keys, self.obs_window)
 
     def _score_importance_real(self, model, input_ids: torch.Tensor) -> torch.Tensor:
-        """Real attention importance from an eager forward pass (nexusquant/pipeline.py:784-836)."""
+        """Real attention importance (nexusquant/pipeline.py:784-836): per layer, the causal
+        softmax of every query against every key, summed over queries, averaged over heads,
+        then averaged over layers.  The forward pass only records each layer's rotated queries
+        and keys; the column sums run on the tensor-core scorer in blocks of 64 queries, so no
+        (b, H, T, T) attention tensor is ever formed.  Models whose attention does not call a
+        module-level ``apply_rotary_pos_emb`` use the reference's eager-attention route."""
+        imp = _real_importance_recorded(model, input_ids)
+        if imp is not None:
+            return imp
         with torch.no_grad():
             out = model(input_ids, use_cache=False, output_attentions=True)
         attentions = out.attentions
@@ -630,6 +638,54 @@ class NexusQuantEvict:
             for l, a, c in zip(grp, ok, ov):
                 _set_layer_kv(past_key_values, l, a, c)
         return past_key_values, mask
+
+
+def _rotary_module(model):
+    """The modeling module whose attention calls a module-level apply_rotary_pos_emb, if any."""
+    import sys
+    for m in model.modules():
+        name = type(m).__name__
+        if name.endswith("Attention"):
+            mod = sys.modules.get(type(m).__module__)
+            if mod is not None and callable(getattr(mod, "apply_rotary_pos_emb", None)):
+                return mod
+    return None
+
+
+def _real_importance_recorded(model, input_ids: torch.Tensor, block: int = 64) -> Optional[torch.Tensor]:
+    """Importance of _score_importance_real from recorded per-layer queries and keys (see there);
+    None when the model's rotary embedding cannot be intercepted."""
+    mod = _rotary_module(model)
+    if mod is None:
+        return None
+    orig = mod.apply_rotary_pos_emb
+    rec = []
+
+    def recording(q, k, *args, **kwargs):
+        qe, ke = orig(q, k, *args, **kwargs)
+        rec.append((qe.detach(), ke.detach()))
+        return qe, ke
+
+    mod.apply_rotary_pos_emb = recording
+    try:
+        with torch.no_grad():
+            model(input_ids, use_cache=False)
+    finally:
+        mod.apply_rotary_pos_emb = orig
+    if not rec:
+        return None
+    b, T = input_ids.shape
+    imp = torch.zeros(b, T, dtype=torch.float32, device=input_ids.device)
+    for q, k in rec:
+        if q.shape[2] != T or k.shape[2] != T:
+            return None  # not a plain prefill of the whole sequence
+        q = q.to(input_ids.device)
+        k = k.to(input_ids.device)
+        for q0 in range(0, T, block):
+            q1 = min(T, q0 + block)  # keys past the block's last query are masked: leave them out
+            part = K.score_attention(q[:, :, q0:q1], k[:, :, :q1], q0)
+            imp[:, :q1] += part
+    return imp / len(rec)
 
 
 def _clip_keep(kept_idx, kept_count, cap, seq_l):

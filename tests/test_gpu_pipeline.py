@@ -186,3 +186,50 @@ def test_evict_host_cache_through_api_matches_device():
             first = out.layers[2].codes.k_codes.data_ptr()
         else:
             assert out.layers[2].codes.k_codes.data_ptr() == first
+
+
+def test_real_scorer_on_model_without_attention_matrix():
+    """scorer='real' on a tiny Llama: the recorded-queries tensor-core route gives the reference's
+    eager-attention importance (fp32 model: within 1e-5) and the same keep mask, and at T = 8192 it
+    runs without forming a (b, H, T, T) attention tensor."""
+    pytest.importorskip("transformers")
+    from transformers import LlamaConfig, LlamaForCausalLM
+    from nexusquant_b200.pipeline import _real_importance_recorded
+    torch.manual_seed(0)
+    cfg = LlamaConfig(vocab_size=128, hidden_size=256, intermediate_size=512, num_hidden_layers=3,
+                      num_attention_heads=4, num_key_value_heads=2, head_dim=64, max_position_embeddings=8192,
+                      attn_implementation="eager")
+    model = LlamaForCausalLM(cfg).to(DEV, torch.float32).eval()
+    ids = torch.randint(0, 128, (2, 300), device=DEV)
+    ours = _real_importance_recorded(model, ids)
+    assert ours is not None
+    with torch.no_grad():
+        att = model(ids, use_cache=False, output_attentions=True).attentions
+    ref = sum(a.float().sum(dim=2).mean(dim=1) for a in att) / len(att)   # pipeline.py:826-835
+    assert torch.allclose(ours, ref, rtol=1e-5, atol=1e-6)
+    ev = nq.NexusQuantEvict(head_dim=64, bits=2, eviction_rate=0.5, sliding_window=16, scorer="real")
+    m_ours = ev._build_keep_mask(ours, 300, 0.5)
+    m_ref = ev._build_keep_mask(ref, 300, 0.5)
+    assert torch.equal(m_ours, m_ref)
+    # long prefill (SDPA forward): memory stays far below one layer's attention tensor
+    ids = torch.randint(0, 128, (1, 8192), device=DEV)
+    cfg.attn_implementation = "sdpa"
+    sdpa = LlamaForCausalLM(cfg)
+    sdpa.load_state_dict(model.state_dict())
+    model = sdpa.to(DEV, torch.float16).eval()
+
+    def peak_of(fn):
+        torch.cuda.synchronize()
+        base = torch.cuda.memory_allocated()
+        torch.cuda.reset_peak_memory_stats()
+        out = fn()
+        torch.cuda.synchronize()
+        return out, torch.cuda.max_memory_allocated() - base
+
+    with torch.no_grad():
+        _, fwd = peak_of(lambda: model(ids, use_cache=False).logits)
+    imp, ours = peak_of(lambda: _real_importance_recorded(model, ids))
+    assert imp.shape == (1, 8192) and torch.isfinite(imp).all()
+    # beyond the forward pass itself: the recorded queries/keys and the scorer's workspace, far
+    # below one fp32 (1, 4, T, T) attention tensor (1 GiB)
+    assert ours - fwd < 128 << 20, (ours, fwd)
