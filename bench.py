@@ -505,6 +505,11 @@ def entropy_leg(cache, cfg, max_tokens: int = 2048) -> dict:
               "cache_ratio_vs_fp16_extrapolated": round(cfg.fp16_bytes / total, 3),
               "bits_per_symbol": round(r["bits_per_symbol"], 4), "delta_seconds": round(r["delta_seconds"], 3),
               "host_seconds": round(r["host_seconds"], 3)})
+    rr = E.rans_report(cache, layers=[q[0]], max_tokens=max_tokens)
+    r["rans"] = {"container": "encode_e8 (entropy_coder.py:405-452), one stream per (K|V, batch)",
+                 "bits_per_symbol": round(rr["bits_per_symbol"], 4), "stream_bytes": rr["stream_bytes"],
+                 "device_seconds": round(rr["device_seconds"], 4), "host_seconds": round(rr["host_seconds"], 4),
+                 "host_msymbols_per_s": round(rr["host_msymbols_per_s"], 1)}
     return r
 
 

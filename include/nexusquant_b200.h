@@ -259,6 +259,30 @@ nq_status_t nq_delta_codes(const uint8_t *codes, int32_t n_streams, int32_t n_to
                            int32_t levels, int8_t *delta, nq_stream_t stream);
 
 /*
+ * rANS entropy coding of the lattice codes (nexusquant/core/entropy_coder.py), split as the
+ * work splits: the symbol and frequency pass over every code runs on the device, only the
+ * inherently serial state loop on the host.
+ *   nq_code_histogram: counts[c + L] += number of codes equal to c, c in [-L, L] (2L + 1
+ *     device uint32 bins, accumulated: zero them first).  An odd code means the stream has
+ *     half-integer lattice coordinates (_lattice_to_symbols, entropy_coder.py:35-75).
+ *   nq_code_symbols: uint8 symbols [rows, d_p] (8-byte aligned), c + L when half != 0 (alphabet
+ *     2L + 1), else c / 2 + L / 2 (alphabet L + 1) -- the reference's shift of doubled or
+ *     integer coordinates.
+ *   nq_rans_encode / nq_rans_decode (HOST pointers, host code): the reference's 32-bit-state,
+ *     16-bit-word rANS with a 12-bit frequency table summing to 4096 (_rans_encode /
+ *     _rans_decode, entropy_coder.py:246-345); words in stream order, *out_len words written,
+ *     NQ_ERR_TOO_LARGE when out_cap is too small (n + 2 words always suffice).
+ */
+nq_status_t nq_code_histogram(const uint8_t *codes, int64_t rows, int32_t head_dim_padded, int32_t levels,
+                              uint32_t *counts, nq_stream_t stream);
+nq_status_t nq_code_symbols(const uint8_t *codes, int64_t rows, int32_t head_dim_padded, int32_t levels,
+                            int32_t half, uint8_t *symbols, nq_stream_t stream);
+nq_status_t nq_rans_encode(const uint8_t *symbols, int64_t n, const uint32_t *freqs, int32_t alphabet,
+                           uint16_t *out, int64_t out_cap, int64_t *out_len);
+nq_status_t nq_rans_decode(const uint16_t *words, int64_t n_words, int64_t n, const uint32_t *freqs,
+                           int32_t alphabet, uint8_t *symbols);
+
+/*
  * Decode attention straight from the compressed layout: one query token per sequence,
  * softmax(q K^T * scale) V with K / V dequantized on the fly as nq_decompress_layers
  * would (keys re-rotated at their positions, sharpened, rounded to fp16), fp16 output.

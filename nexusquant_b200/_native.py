@@ -96,6 +96,10 @@ _PROTOS = {
     "nq_gather_rows": (c_i32, [c_vp, c_i32, c_i32, c_i32, c_i32, c_i64, c_i64, c_i64, c_vp, c_vp, c_i32, c_vp,
                                c_i64, c_i64, c_i64, c_vp]),
     "nq_delta_codes": (c_i32, [c_vp, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp]),
+    "nq_code_histogram": (c_i32, [c_vp, c_i64, c_i32, c_i32, c_vp, c_vp]),
+    "nq_code_symbols": (c_i32, [c_vp, c_i64, c_i32, c_i32, c_i32, c_vp, c_vp]),
+    "nq_rans_encode": (c_i32, [c_vp, c_i64, c_vp, c_i32, c_vp, c_i64, ctypes.POINTER(c_i64)]),
+    "nq_rans_decode": (c_i32, [c_vp, c_i64, c_i64, c_vp, c_i32, c_vp]),
     "nq_attend_compressed_workspace_size": (c_size, [c_i32, c_i32, c_i32, c_i32]),
     "nq_attend_compressed": (c_i32, [ctypes.POINTER(AttendParams), c_vp, c_size, c_vp]),
     "nq_merge_centroid_accumulate": (c_i32, [ctypes.POINTER(c_vp), c_i32, c_i32, c_i32, c_i32, c_i32, c_i64,

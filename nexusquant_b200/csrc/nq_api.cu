@@ -302,6 +302,81 @@ nq_status_t nq_delta_codes(const uint8_t* codes, int32_t n_streams, int32_t n_to
       nq::launch_delta(codes, n_streams, n_tokens, head_dim_padded, levels, delta, static_cast<cudaStream_t>(stream)));
 }
 
+nq_status_t nq_code_histogram(const uint8_t* codes, int64_t rows, int32_t head_dim_padded, int32_t levels,
+                              uint32_t* counts, nq_stream_t stream) {
+  if (!codes || !counts || rows < 0 || !valid_levels(levels)) return NQ_ERR_INVALID_ARG;
+  if (head_dim_padded <= 0 || (head_dim_padded & 7)) return NQ_ERR_INVALID_ARG;
+  return cuda_status(nq::launch_code_symbols(codes, rows, head_dim_padded, levels, 0, 0, counts, nullptr,
+                                             static_cast<cudaStream_t>(stream)));
+}
+
+nq_status_t nq_code_symbols(const uint8_t* codes, int64_t rows, int32_t head_dim_padded, int32_t levels,
+                            int32_t half, uint8_t* symbols, nq_stream_t stream) {
+  if (!codes || !symbols || rows < 0 || !valid_levels(levels)) return NQ_ERR_INVALID_ARG;
+  if (head_dim_padded <= 0 || (head_dim_padded & 7)) return NQ_ERR_INVALID_ARG;
+  if (reinterpret_cast<uintptr_t>(symbols) & 7) return NQ_ERR_ALIGNMENT;
+  return cuda_status(nq::launch_code_symbols(codes, rows, head_dim_padded, levels, 1, half != 0, nullptr, symbols,
+                                             static_cast<cudaStream_t>(stream)));
+}
+
+// rANS, 32-bit state, 16-bit words, M = 2^12, state in [2^16, 2^32)
+// (nexusquant/core/entropy_coder.py:246-295 encode, :298-345 decode).  Host code.
+nq_status_t nq_rans_encode(const uint8_t* symbols, int64_t n, const uint32_t* freqs, int32_t alphabet,
+                           uint16_t* out, int64_t out_cap, int64_t* out_len) {
+  if ((!symbols && n) || !freqs || !out || !out_len || alphabet <= 0 || alphabet > 256 || n < 0) return NQ_ERR_INVALID_ARG;
+  uint32_t cum[257];
+  cum[0] = 0;
+  for (int s = 0; s < alphabet; ++s) cum[s + 1] = cum[s] + freqs[s];
+  if (cum[alphabet] != 4096u) return NQ_ERR_INVALID_ARG;
+  int64_t k = 0;  // words written, in reverse order
+  uint64_t state = 1u << 16;
+  for (int64_t i = n - 1; i >= 0; --i) {
+    const unsigned s = symbols[i];
+    if (s >= (unsigned)alphabet || freqs[s] == 0) return NQ_ERR_INVALID_ARG;
+    const uint64_t fs = freqs[s];
+    const uint64_t threshold = fs << 20;
+    while (state >= threshold) {
+      if (k >= out_cap) return NQ_ERR_TOO_LARGE;
+      out[k++] = (uint16_t)(state & 0xFFFFu);
+      state >>= 16;
+    }
+    state = (state / fs) * 4096u + (state % fs) + cum[s];
+  }
+  if (k + 2 > out_cap) return NQ_ERR_TOO_LARGE;
+  out[k++] = (uint16_t)(state & 0xFFFFu);
+  out[k++] = (uint16_t)((state >> 16) & 0xFFFFu);
+  for (int64_t a = 0, b = k - 1; a < b; ++a, --b) {
+    const uint16_t t = out[a];
+    out[a] = out[b];
+    out[b] = t;
+  }
+  *out_len = k;
+  return NQ_OK;
+}
+
+nq_status_t nq_rans_decode(const uint16_t* words, int64_t n_words, int64_t n, const uint32_t* freqs,
+                           int32_t alphabet, uint8_t* symbols) {
+  if (!words || n_words < 2 || !freqs || (!symbols && n) || alphabet <= 0 || alphabet > 256 || n < 0)
+    return NQ_ERR_INVALID_ARG;
+  uint32_t cum[257];
+  cum[0] = 0;
+  for (int s = 0; s < alphabet; ++s) cum[s + 1] = cum[s] + freqs[s];
+  if (cum[alphabet] != 4096u) return NQ_ERR_INVALID_ARG;
+  static thread_local uint8_t slot2sym[4096];
+  for (int s = 0; s < alphabet; ++s)
+    for (uint32_t c = cum[s]; c < cum[s + 1]; ++c) slot2sym[c] = (uint8_t)s;
+  int64_t pos = 2;
+  uint64_t state = ((uint64_t)words[0] << 16) | words[1];
+  for (int64_t i = 0; i < n; ++i) {
+    const uint32_t slot = (uint32_t)(state & 4095u);
+    const unsigned s = slot2sym[slot];
+    state = freqs[s] * (state >> 12) + slot - cum[s];
+    while (state < (1u << 16) && pos < n_words) state = (state << 16) | words[pos++];
+    symbols[i] = (uint8_t)s;
+  }
+  return NQ_OK;
+}
+
 }  // extern "C"
 
 extern "C" {

@@ -104,6 +104,8 @@ cudaError_t launch_select(const float* imp, int batch, int seq, int sliding_wind
 cudaError_t launch_gather_rows(const void* in, int dtype, int batch, int heads, int head_dim, int64_t isb,
                                int64_t ish, int64_t ist, const int32_t* kept_idx, const int32_t* kept_count,
                                int n_kept, uint16_t* out, int64_t osb, int64_t osh, int64_t ost, cudaStream_t s);
+cudaError_t launch_code_symbols(const uint8_t* codes, int64_t rows, int dp, int levels, int mode, int half,
+                                unsigned int* counts, uint8_t* symbols, cudaStream_t s);
 cudaError_t launch_delta(const uint8_t* codes, int n_streams, int n_tokens, int dp, int levels, int8_t* delta,
                          cudaStream_t s);
 

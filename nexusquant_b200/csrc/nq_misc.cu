@@ -112,4 +112,63 @@ cudaError_t launch_delta(const uint8_t* codes, int n_streams, int n_tokens, int 
   return cudaGetLastError();
 }
 
+// rANS symbol pass (nexusquant/core/entropy_coder.py:35-75 applied to the lattice codes).
+// mode 0: counts[c + L] += #rows with code c (c in [-L, L]; 2L + 1 bins, shared-memory
+//         histogram per CTA, one global atomic per bin and CTA).
+// mode 1: symbols[i] = half ? c + L : c / 2 + L / 2 (uint8, row-major [rows, d_p]), the
+//         reference's shift for half-integer (doubled) or integer coordinates.
+// Symbols are clipped to the alphabet as the reference clips them.
+__device__ __forceinline__ uint32_t rans_symbol(int c, int levels, int half) {
+  return half ? (uint32_t)min(max(c + levels, 0), 2 * levels)
+              : (uint32_t)min(max((c >> 1) + levels / 2, 0), levels);
+}
+
+__global__ void code_symbols_kernel(const uint8_t* codes, int64_t rows, int dp, int levels, int mode, int half,
+                                    unsigned int* counts, uint8_t* symbols) {
+  __shared__ unsigned int h[33];
+  if (mode == 0)
+    for (int i = threadIdx.x; i < 33; i += blockDim.x) h[i] = 0;
+  __syncthreads();
+  const int G = dp / 8;
+  const int pb = levels <= 4 ? dp / 2 : (levels == 8 ? dp * 5 / 8 : dp);
+  const int64_t total = rows * G;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = i / G;
+    const int g = (int)(i - row * G);
+    int c[8];
+    unpack_group(codes + row * pb, g, levels, c);
+    if (mode == 0) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) atomicAdd(&h[min(max(c[k] + levels, 0), 2 * levels)], 1u);
+    } else {
+      uint32_t lo = 0, hi = 0;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        lo |= rans_symbol(c[k], levels, half) << (8 * k);
+        hi |= rans_symbol(c[4 + k], levels, half) << (8 * k);
+      }
+      *reinterpret_cast<uint2*>(symbols + row * dp + 8 * g) = make_uint2(lo, hi);
+    }
+  }
+  if (mode == 0) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < 2 * levels + 1; i += blockDim.x)
+      if (h[i]) atomicAdd(&counts[i], h[i]);
+  }
+}
+
+cudaError_t launch_code_symbols(const uint8_t* codes, int64_t rows, int dp, int levels, int mode, int half,
+                                unsigned int* counts, uint8_t* symbols, cudaStream_t s) {
+  const int64_t total = rows * (dp / 8);
+  if (total == 0) return cudaSuccess;
+  int dev = 0, sms = 0;
+  cudaError_t e;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+  if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+  long long grid = (total + 255) / 256;
+  if (grid > 8LL * sms) grid = 8LL * sms;
+  code_symbols_kernel<<<(unsigned)grid, 256, 0, s>>>(codes, rows, dp, levels, mode, half, counts, symbols);
+  return cudaGetLastError();
+}
+
 }  // namespace nq

@@ -223,3 +223,171 @@ def entropy_report(cache, level: int = 22, codec: str = "auto", threads: int = 0
         "sampled": layers is not None or max_tokens is not None,
     }
     return out
+
+
+# ------------------------------------------------------------------------------ rANS
+# The reference's rANS container for E8 lattice codes (nexusquant/core/entropy_coder.py):
+#   header '<IBBI' (n_groups, levels, has_half, n_symbols), '<III' section lengths,
+#   frequency table ('<H' alphabet size, '<H' per symbol), fp16 scale per 8-group,
+#   rANS words ('<H', 32-bit state, 16-bit renormalisation, 12-bit table).
+# The symbol mapping and the histogram over every code run on the device
+# (kernels.code_histogram / kernels.code_symbols); the table normalisation is a few dozen
+# numbers and the state loop is serial, both on the host (the loop in native code).
+RANS_PROB_BITS = 12
+RANS_M = 1 << RANS_PROB_BITS
+RANS_HEADER = "<IBBI"
+RANS_LENGTHS = "<III"
+
+
+def rans_freq_table(counts: np.ndarray) -> np.ndarray:
+    """Normalised frequencies summing to 4096 from symbol counts, as _build_freq_table
+    (entropy_coder.py:175-243): every seen symbol gets 1, the rest of the budget is shared
+    by floor(count / total * remaining), leftovers go to the largest fractional parts in
+    numpy argsort order (the same sort calls, so ties break the same way)."""
+    counts = np.asarray(counts, dtype=np.int64)
+    a = counts.size
+    total = int(counts.sum())
+    if total == 0:
+        freqs = np.full(a, RANS_M // a, dtype=np.int64)
+        freqs[0] += RANS_M - int(freqs.sum())
+        return freqs
+    seen = counts > 0
+    n_seen = int(seen.sum())
+    freqs = np.zeros(a, dtype=np.int64)
+    freqs[seen] = 1
+    remaining = RANS_M - n_seen
+    seen_idx = np.where(seen)[0]
+    if remaining > 0:
+        share = (counts[seen].astype(np.float64) / total) * remaining
+        extra = np.floor(share).astype(np.int64)
+        freqs[seen] += extra
+        diff = int(RANS_M - freqs.sum())
+        if diff > 0:
+            order = seen_idx[np.argsort(-(share - extra))]
+            for i in range(diff):
+                freqs[order[i % len(order)]] += 1
+        elif diff < 0:
+            order = seen_idx[np.argsort(counts[seen])]
+            removed = 0
+            for j in order:
+                while freqs[j] > 1 and removed < -diff:
+                    freqs[j] -= 1
+                    removed += 1
+                if removed >= -diff:
+                    break
+    elif remaining < 0:  # more seen symbols than table slots: unreachable for alphabets <= 33
+        order = seen_idx[np.argsort(-counts[seen])]
+        freqs[:] = 0
+        freqs[order[:RANS_M]] = 1
+    if int(freqs.sum()) != RANS_M:
+        raise ValueError(f"frequency table sums to {int(freqs.sum())}, not {RANS_M}")
+    return freqs
+
+
+def rans_encode(symbols: np.ndarray, freqs: np.ndarray) -> np.ndarray:
+    """rANS words (uint16, stream order) of uint8 symbols (_rans_encode, entropy_coder.py:246-295);
+    the state loop runs in the native library."""
+    from . import _native as N
+    sym = np.ascontiguousarray(symbols, dtype=np.uint8).reshape(-1)
+    fr = np.ascontiguousarray(freqs, dtype=np.uint32)
+    out = np.empty(sym.size + 2, dtype=np.uint16)
+    n_out = ctypes.c_int64(0)
+    N.call("nq_rans_encode", sym.ctypes.data, sym.size, fr.ctypes.data, fr.size, out.ctypes.data, out.size,
+           ctypes.byref(n_out))
+    return out[:n_out.value].copy()
+
+
+def rans_decode(words: np.ndarray, n_symbols: int, freqs: np.ndarray) -> np.ndarray:
+    """Inverse of rans_encode (_rans_decode, entropy_coder.py:298-345)."""
+    from . import _native as N
+    w = np.ascontiguousarray(words, dtype=np.uint16)
+    fr = np.ascontiguousarray(freqs, dtype=np.uint32)
+    out = np.empty(int(n_symbols), dtype=np.uint8)
+    N.call("nq_rans_decode", w.ctypes.data, w.size, out.size, fr.ctypes.data, fr.size, out.ctypes.data)
+    return out
+
+
+def rans_pack_e8(symbols: np.ndarray, counts: np.ndarray, has_half: bool, levels: int,
+                 group_scales: np.ndarray) -> bytes:
+    """The encode_e8 byte stream (entropy_coder.py:405-452) from symbols already mapped,
+    their counts over the alphabet and one fp16 scale per 8-group."""
+    sym = np.ascontiguousarray(symbols, dtype=np.uint8).reshape(-1)
+    freqs = rans_freq_table(counts)
+    words = rans_encode(sym, freqs)
+    scales = np.ascontiguousarray(group_scales, dtype=np.float16).reshape(-1)
+    n_groups = scales.size
+    if sym.size != 8 * n_groups:
+        raise ValueError(f"{sym.size} symbols for {n_groups} groups of 8")
+    ftab = struct.pack("<H", freqs.size) + freqs.astype("<u2").tobytes()
+    sc = scales.astype("<f2").tobytes()
+    wd = words.astype("<u2").tobytes()
+    return (struct.pack(RANS_HEADER, n_groups, int(levels), int(bool(has_half)), sym.size) +
+            struct.pack(RANS_LENGTHS, len(ftab), len(sc), len(wd)) + ftab + sc + wd)
+
+
+def rans_encode_e8(packed: torch.Tensor, row_scales: torch.Tensor, head_dim_padded: int, levels: int,
+                   timings: Optional[dict] = None) -> bytes:
+    """encode_e8 (entropy_coder.py:405-452) of packed code rows [..., pb] with one fp16
+    scale per row [...]: the stream the reference writes for quantized = code / 2 * scale and
+    that row's scale repeated over its 8-groups.  Histogram and symbols on the device;
+    ``timings`` (if given) accumulates 'device_seconds' (passes + copies) and 'host_seconds'."""
+    t0 = time.perf_counter()
+    cnt = K.code_histogram(packed, head_dim_padded, levels).cpu().numpy().astype(np.int64)
+    has_half = bool(cnt[1::2].sum() > 0)   # L is even: bin c + L is odd exactly for odd (half-integer) c
+    sym = K.code_symbols(packed, head_dim_padded, levels, has_half).cpu().numpy()
+    alpha = cnt if has_half else cnt[0::2]
+    g = head_dim_padded // 8
+    sc = row_scales.reshape(-1, 1).expand(-1, g).reshape(-1).cpu().numpy()
+    t1 = time.perf_counter()
+    blob = rans_pack_e8(sym, alpha, has_half, levels, sc)
+    if timings is not None:
+        timings["device_seconds"] = timings.get("device_seconds", 0.0) + t1 - t0
+        timings["host_seconds"] = timings.get("host_seconds", 0.0) + time.perf_counter() - t1
+    return blob
+
+
+def rans_report(cache, layers=None, max_tokens: Optional[int] = None) -> Dict[str, float]:
+    """rANS-coded size (encode_e8 container, one stream per (layer, K|V, batch) of the kept
+    tokens) of a CompressedKVCache's codes; ``layers`` / ``max_tokens`` sample it."""
+    cnt = cache.kept_count.cpu().tolist()
+    idx = range(len(cache.layers)) if layers is None else layers
+    dev = torch.device("cuda", torch.cuda.current_device())
+    tm: dict = {}
+    n_sym = n_bytes = 0
+    for li in idx:
+        c = cache.layers[li].codes
+        if c is None:
+            continue
+        for packed, scales, lev in ((c.k_codes, c.k_scales, c.key_levels), (c.v_codes, c.v_scales, c.value_levels)):
+            n = packed.shape[2]
+            for bi in range(packed.shape[0]):
+                m = min(cnt[bi], n) if max_tokens is None else min(cnt[bi], n, max_tokens)
+                if m <= 0:
+                    continue
+                blob = rans_encode_e8(packed[bi, :, :m].to(dev), scales[bi, :, :m].to(dev),
+                                      cache.head_dim_padded, lev, tm)
+                n_sym += packed.shape[1] * m * cache.head_dim_padded
+                n_bytes += len(blob)
+    return {"symbols": n_sym, "stream_bytes": n_bytes,
+            "bits_per_symbol": 8.0 * n_bytes / n_sym if n_sym else 0.0,
+            "device_seconds": tm.get("device_seconds", 0.0), "host_seconds": tm.get("host_seconds", 0.0),
+            "host_msymbols_per_s": n_sym / tm["host_seconds"] / 1e6 if tm.get("host_seconds") else 0.0}
+
+
+def rans_decode_e8(data: bytes):
+    """Inverse of the encode_e8 stream (decode_e8, entropy_coder.py:455-500) ->
+    (doubled lattice codes int8 [n_groups * 8], fp16 scales [n_groups])."""
+    off = 0
+    n_groups, levels, has_half, n_sym = struct.unpack_from(RANS_HEADER, data, off)
+    off += struct.calcsize(RANS_HEADER)
+    flen, slen, rlen = struct.unpack_from(RANS_LENGTHS, data, off)
+    off += struct.calcsize(RANS_LENGTHS)
+    a = struct.unpack_from("<H", data, off)[0]
+    freqs = np.frombuffer(data, dtype="<u2", count=a, offset=off + 2).astype(np.uint32)
+    off += flen
+    scales = np.frombuffer(data, dtype="<f2", count=slen // 2, offset=off).copy()
+    off += slen
+    words = np.frombuffer(data, dtype="<u2", count=rlen // 2, offset=off)
+    sym = rans_decode(words, n_sym, freqs).astype(np.int32)
+    codes = (sym - levels) if has_half else 2 * (sym - levels // 2)
+    return codes.astype(np.int8), scales

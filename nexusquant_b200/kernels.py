@@ -524,6 +524,33 @@ def delta_codes(codes: torch.Tensor, head_dim_padded: int, levels: int) -> torch
     return out
 
 
+def code_histogram(codes: torch.Tensor, head_dim_padded: int, levels: int,
+                   counts: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Histogram of the doubled lattice codes of packed rows [..., pb]: int32 [2L + 1] with
+    counts[c + L] = number of codes equal to c (accumulated into ``counts`` when given)."""
+    _require_cuda(codes)
+    codes = codes.contiguous()
+    rows = codes.numel() // max(codes.shape[-1], 1)
+    if counts is None:
+        counts = torch.zeros(2 * levels + 1, dtype=torch.int32, device=codes.device)
+    N.call("nq_code_histogram", codes.data_ptr(), rows, head_dim_padded, int(levels), counts.data_ptr(),
+           _stream(codes.device))
+    return counts
+
+
+def code_symbols(codes: torch.Tensor, head_dim_padded: int, levels: int, half: bool) -> torch.Tensor:
+    """rANS symbols (nexusquant/core/entropy_coder.py:35-75) of packed rows [..., pb] ->
+    uint8 [..., d_p]: c + L with half-integer coordinates present, else c / 2 + L / 2."""
+    _require_cuda(codes)
+    codes = codes.contiguous()
+    *lead, pb = codes.shape
+    rows = codes.numel() // max(pb, 1)
+    out = torch.empty((*lead, head_dim_padded), dtype=torch.uint8, device=codes.device)
+    N.call("nq_code_symbols", codes.data_ptr(), rows, head_dim_padded, int(levels), int(bool(half)),
+           out.data_ptr(), _stream(codes.device))
+    return out
+
+
 # ---------------------------------------------------------------------------
 # Names of the reference's GPU wrappers (nexusquant/kernels/e8_triton.py)
 # ---------------------------------------------------------------------------

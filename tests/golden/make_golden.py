@@ -3,7 +3,7 @@
 Run in a container that has the reference checked out (read-only is fine):
 
     PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py --ref /path/to/nexusquant
-    (--part merge regenerates only merge.npz)
+    (--part merge / entropy / rans regenerates only merge.npz / entropy.npz / rans.npz)
 
 The reference is jagmarques/nexusquant v0.5.0.  Every fixture is produced by the
 reference's own functions on seeded inputs (nexusquant_b200.synthetic or small
@@ -148,12 +148,50 @@ def make_entropy() -> dict:
     return fx
 
 
+RANS_CASES = (("l4", 4, 48, 0), ("l4even", 4, 48, 1), ("l2", 2, 40, 0), ("l8", 8, 24, 0), ("l16", 16, 24, 0),
+              ("zero", 4, 8, 2))
+
+
+def rans_case(levels, rows, kind, seed=7):
+    """Seeded E8 codes of ``rows`` Gaussian rows (d = d_p = 128) from the C oracle's quantizer,
+    with fp16 scales; kind 1 clears the low bit (integer coordinates only), kind 2 zeroes all."""
+    rng = np.random.default_rng(seed + 131 * levels + rows)
+    x = rng.standard_normal((rows, 128)).astype(np.float32)
+    codes, scales = orc.quantize(x, 128, levels)
+    if kind == 1:
+        codes = (codes & ~1).astype(np.int8)
+    elif kind == 2:
+        codes = np.zeros_like(codes)
+    return codes, scales.astype(np.float16)
+
+
+def make_rans() -> dict:
+    """entropy_coder.encode_e8 (entropy_coder.py:405-452) run by the reference on
+    quantized = code / 2 * scale with the row's fp16 scale repeated over its 8-groups, and
+    decode_e8's round trip."""
+    from nexusquant.core import entropy_coder as EC
+    fx = {}
+    for name, levels, rows, kind in RANS_CASES:
+        codes, s16 = rans_case(levels, rows, kind)
+        sc = np.repeat(s16.astype(np.float32), 128 // 8)
+        q = torch.from_numpy(codes.astype(np.float32).reshape(-1, 8) / 2.0 * sc[:, None])
+        blob = EC.encode_e8(q, torch.from_numpy(sc), levels=levels)
+        dq, ds = EC.decode_e8(blob)
+        fx[f"{name}_codes"] = codes
+        fx[f"{name}_scales"] = s16
+        fx[f"{name}_levels"] = np.int64(levels)
+        fx[f"{name}_stream"] = np.frombuffer(blob, np.uint8)
+        fx[f"{name}_roundtrip"] = np.int64(int(torch.equal(dq.reshape(-1, 8).float(), q)))
+    return fx
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("NQ_REFERENCE"),
                     help="checkout of the reference (or set NQ_REFERENCE)")
-    ap.add_argument("--part", choices=["all", "merge", "entropy"], default="all",
-                    help="merge: write only merge.npz (merge eviction fixtures); entropy: only entropy.npz")
+    ap.add_argument("--part", choices=["all", "merge", "entropy", "rans"], default="all",
+                    help="merge: write only merge.npz (merge eviction fixtures); entropy: only entropy.npz; "
+                         "rans: only rans.npz")
     args = ap.parse_args()
     if not args.ref:
         ap.error("--ref (or NQ_REFERENCE) must name the reference checkout")
@@ -161,6 +199,11 @@ def main():
     if args.part == "entropy":
         out = os.path.join(HERE, "entropy.npz")
         np.savez_compressed(out, **make_entropy())
+        print("wrote", out, os.path.getsize(out), "bytes")
+        return
+    if args.part == "rans":
+        out = os.path.join(HERE, "rans.npz")
+        np.savez_compressed(out, **make_rans())
         print("wrote", out, os.path.getsize(out), "bytes")
         return
     if args.part == "merge":
