@@ -7,13 +7,22 @@
 // heads (q head g*G .. g*G+G-1 reads KV head g; G = 1 is the reference's case).
 //
 // Split-K over tokens, two kernels:
-//  * attend_partial: CTA = (token split, KV head, batch), 128 threads.  Per tile of 128
-//    tokens each thread decodes one key in registers (unpack -> exact half2 butterfly ->
-//    scale -> RoPE -> sharpen -> fp16, as the dequantize kernel) and dots it with the G
-//    queries (base-2 logits).  Values stay in the code domain: because the inverse
-//    Hadamard is linear, sum_t p_t v_t = h/2 * H^T (sum_t p_t s_t c_t), so the CTA
-//    accumulates p_t * scale_t * codes_t per dimension (thread j owns dimension j) with
-//    online-softmax rescaling, and writes (max, sum, accumulator) per query head.
+//  * attend_partial: CTA = (token split, KV head, batch), 128 threads, both contractions on
+//    the 5th-generation tensor cores (tcgen05.mma kind::f16, fp32 accumulators in TMEM).
+//    Per tile of 128 tokens:
+//      - thread t decodes key t in registers (unpack -> exact half2 butterfly -> scale ->
+//        RoPE -> sharpen -> fp16, the dequantize kernel's arithmetic) into a K-major,
+//        128-byte-swizzled shared tile, and converts value t's codes (small integers, exact
+//        in fp16) into an MN-major swizzled tile;
+//      - one thread issues S = K Q^T (M = 128 tokens, N = 16 >= G query heads, K = 128);
+//        thread t reads its token's logits back from TMEM lane t;
+//      - online softmax over the tile; the weights p_t * s_t (value scale) go to shared
+//        memory as fp16;
+//      - one thread issues O = C^T W^T (M = 128 dimensions, N = 16, K = 128 tokens): values
+//        stay in the code domain because the inverse Hadamard is linear,
+//        sum_t p_t v_t = h/2 * H^T (sum_t p_t s_t c_t); thread j reads dimension j from
+//        TMEM and folds it into its running accumulator with the softmax rescale.
+//    It writes (max, sum, accumulator) per query head and split.
 //  * attend_combine: per (batch, query head) merges the splits, divides by the softmax
 //    sum, applies the inverse Walsh-Hadamard butterfly once and scales by h/2.
 // Fixed reduction orders throughout: deterministic.
@@ -21,6 +30,7 @@
 
 #include "nq_common.cuh"
 #include "nq_internal.h"
+#include "nq_umma.cuh"
 
 namespace nq {
 
@@ -96,59 +106,115 @@ __device__ __forceinline__ void at_unpack(const uint8_t* p, __half2 (&R)[64]) {
   }
 }
 
-// Code (integer) of coordinate j of a packed row.
-template <int FMT>
-__device__ __forceinline__ int at_code(const uint8_t* row, int j) {
-  if constexpr (FMT == 0) return (int)((row[j >> 1] >> ((j & 1) * 4)) & 0xF) - 8;
-  else if constexpr (FMT == 1) {
-    const int bit = 5 * j, byte = bit >> 3, s = bit & 7;
-    const uint32_t v = (uint32_t)row[byte] | (s > 3 ? ((uint32_t)row[byte + 1] << 8) : 0u);  // stays in the row
-    return (int)((v >> s) & 0x1F) - 8;
-  } else {
-    return (int)(int8_t)row[j];
-  }
-}
-
 template <int FMT>
 constexpr int at_pb() { return FMT == 0 ? 64 : (FMT == 1 ? 80 : 128); }
 
 }  // namespace
 
 
-// 3 CTAs per SM: the register cap (170) costs 16 bytes of spill at G = 8 and lifts occupancy
-// from 8 to 12 warps; the kernel is latency-bound (scoreboard stalls), and on B200 this is
-// 83 us against 93 us at 2 CTAs for a config-4 layer.  attend_splits sizes the grid to one wave.
+// Device error word of the attention kernel's bounded waits (bit 2 of nq_device_error).
+__device__ unsigned int g_attend_wait_error;
+
+// Shared-memory plan of attend_partial (offsets from a 1024-byte aligned base).
+struct AtSmem {
+  static constexpr int kK = 0;          // keys: 2 column blocks x 128 rows x 128 B, K-major SW128
+  static constexpr int kV = 32768;      // value codes: 2 M blocks (64 dims) x 16 groups of 8 tokens x 1024 B
+  static constexpr int kQ = 65536;      // queries: 2 column blocks x 16 rows x 128 B
+  static constexpr int kW = 69632;      // weights: 2 token blocks x 16 rows x 128 B
+  static constexpr int kBytes = 73728 + 1024;  // + alignment slack
+  static constexpr int kN = 16;         // MMA N (query heads, zero rows above G)
+};
+
+// Byte offset of element (row, col) of a K-major SW128 operand with 128-byte rows grouped
+// in column blocks of 64 elements (block stride `blk`): 16-byte chunk index XOR row % 8.
+__device__ __forceinline__ uint32_t sw128_off(int row, int col, int blk) {
+  return (uint32_t)((col >> 6) * blk + row * 128 + ((((col & 63) >> 3) ^ (row & 7)) << 4) + (col & 7) * 2);
+}
+
+// Value codes of dimensions 2p, 2p + 1 as a half2 of exact integers, from a packed row in words.
+template <int FMT>
+__device__ __forceinline__ uint32_t at_code_pair(const uint32_t* w, int p) {
+  if constexpr (FMT == 0) {
+    // byte p holds dimensions 2p (low nibble) and 2p + 1 (high nibble): [byte, 0, byte, 0]
+    const uint32_t x = __byte_perm(w[p >> 2], 0u, 0x4040u + (uint32_t)(p & 3) * 0x0101u);
+    const __half2 h = __hfma2(ah2_bits((x & 0x00F0000Fu) | 0x64006400u), __floats2half2_rn(1.0f, 1.0f / 16.0f),
+                              __floats2half2_rn(-1032.0f, -72.0f));
+    return *reinterpret_cast<const uint32_t*>(&h);
+  } else if constexpr (FMT == 1) {
+    uint32_t f[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int bit = 5 * (2 * p + e), k = bit >> 5, sh = bit & 31;
+      f[e] = (sh + 5 <= 32 ? (w[k] >> sh) : __funnelshift_r(w[k], w[k + 1], sh)) & 31u;
+    }
+    const __half2 h = __hadd2(ah2_bits(f[0] | (f[1] << 16) | 0x64006400u), ah2c(-1032.0f));
+    return *reinterpret_cast<const uint32_t*>(&h);
+  } else {
+    const uint32_t x = __byte_perm(w[p >> 1], 0u, (p & 1) ? 0x4342u : 0x4140u);
+    const __half2 h = __hadd2(ah2_bits((x ^ 0x00800080u) | 0x64006400u), ah2c(-1152.0f));
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+}
+
+#ifndef AT_ROPE_BATCH
+#define AT_ROPE_BATCH 8  // RoPE values (cos and sin) fetched per batch in the key decode
+#endif
+
+// 3 CTAs per SM (74 KB of shared memory each), one wave (attend_splits).
 template <int FMTK, int FMTV, int G>
 __global__ void __launch_bounds__(kAtTok, 3) attend_partial(const AttendArgs a) {
   constexpr int PBV = at_pb<FMTV>();
-  __shared__ float qs[G][kAtD];                     // queries * scale * log2 e
-  __shared__ __align__(16) uint8_t vrow[kAtTok][PBV];  // value codes of the tile
-  __shared__ float wgt[G][kAtTok];                  // p_t * value scale_t
+  extern __shared__ uint8_t at_smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(at_smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* kb = sm + AtSmem::kK;
+  uint8_t* vb = sm + AtSmem::kV;
+  uint8_t* qb = sm + AtSmem::kQ;
+  uint8_t* wb = sm + AtSmem::kW;
+  __shared__ uint64_t barS, barO;
+  __shared__ uint32_t tmem_base;
   __shared__ float red[G][4];
+  __shared__ int err;
   const int split = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int count = a.count ? min(a.count[b], a.n_tokens) : a.n_tokens;
   const int t0 = split * a.tokens_per_split, t1 = min(count, t0 + a.tokens_per_split);
   const float qscale = a.scale * kAtLog2e;
+
+  // queries (fp16, exact) and the zero rows G..15 of the query and weight operands
+  for (int e = tid; e < (AtSmem::kW + 4096 - AtSmem::kQ) / 16; e += kAtTok)
+    reinterpret_cast<uint4*>(qb)[e] = make_uint4(0u, 0u, 0u, 0u);
+  if (tid == 0) {
+    mbar_init(&barS, 1);
+    mbar_init(&barO, 1);
+    fence_mbar_init();
+    err = 0;
+  }
+  if (warp == 0) tmem_alloc(&tmem_base, 32);
+  __syncthreads();
   for (int e = tid; e < G * kAtD; e += kAtTok) {
     const int g = e / kAtD, j = e % kAtD;
-    qs[g][j] = __half2float(a.q[(int64_t)b * a.q_stride_b + (int64_t)(kh * G + g) * a.q_stride_h + j]) * qscale;
+    *reinterpret_cast<__half*>(qb + sw128_off(g, j, 2048)) =
+        a.q[(int64_t)b * a.q_stride_b + (int64_t)(kh * G + g) * a.q_stride_h + j];
   }
-  float m[G], l[G], acc[G];
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tS = tmem_base, tO = tmem_base + 16;
+  const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+  constexpr uint32_t kIdescQK = f16_idesc(0, 128, AtSmem::kN);
+  constexpr uint32_t kIdescPV = f16_idesc(0, 128, AtSmem::kN) | (1u << 15);  // A (value codes) MN-major
+
+  float m[G], lsum[G], acc[G];
 #pragma unroll
-  for (int g = 0; g < G; ++g) { m[g] = -INFINITY; l[g] = 0.0f; acc[g] = 0.0f; }
+  for (int g = 0; g < G; ++g) { m[g] = -INFINITY; lsum[g] = 0.0f; acc[g] = 0.0f; }
   const int64_t row0 = ((int64_t)b * a.heads + kh) * a.n_tokens;
   const float coef_h = 0.5f * hadamard_entry(kAtD);
-  __syncthreads();
-  for (int base = t0; base < t1; base += kAtTok) {
+  uint32_t ph = 0;
+  for (int base = t0; base < t1; base += kAtTok, ph ^= 1u) {
     const int t = base + tid;
     const bool valid = t < t1;
-    float s[G];
-#pragma unroll
-    for (int g = 0; g < G; ++g) s[g] = -INFINITY;
-    float sv = 0.0f;
+    // ---- key t -> row tid of the key tile (fp16, the dequantize kernel's values)
     if (valid) {
-      // key: decode as the dequantize kernel does, then dot with the queries
       __half2 R[64];
       at_unpack<FMTK>(a.k_codes + (row0 + t) * at_pb<FMTK>(), R);
 #pragma unroll
@@ -167,36 +233,102 @@ __global__ void __launch_bounds__(kAtTok, 3) attend_partial(const AttendArgs a) 
       const int pos = min(max(a.positions[(int64_t)b * a.n_tokens + t], 0), a.rope_rows - 1);
       const float* cs = a.rope_cos + (int64_t)pos * (kAtD / 2);
       const float* sn = a.rope_sin + (int64_t)pos * (kAtD / 2);
+      const u64 coef2 = pk(coef, coef), sh2 = pk(a.key_sharpen, a.key_sharpen);
 #pragma unroll
-      for (int g = 0; g < G; ++g) s[g] = 0.0f;
+      for (int i0 = 0; i0 < 64; i0 += AT_ROPE_BATCH) {
+        // one batch of RoPE rows in flight at a time
+        float cb[AT_ROPE_BATCH], sb[AT_ROPE_BATCH];
 #pragma unroll
-      for (int i = 0; i < 64; i += 4) {
-        const float4 c4 = __ldg(reinterpret_cast<const float4*>(cs + i));
-        const float4 s4 = __ldg(reinterpret_cast<const float4*>(sn + i));
-        const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, ss[4] = {s4.x, s4.y, s4.z, s4.w};
+        for (int k = 0; k < AT_ROPE_BATCH; k += 4) {
+          const float4 c4 = __ldg(reinterpret_cast<const float4*>(cs + i0 + k));
+          const float4 s4 = __ldg(reinterpret_cast<const float4*>(sn + i0 + k));
+          cb[k] = c4.x; cb[k + 1] = c4.y; cb[k + 2] = c4.z; cb[k + 3] = c4.w;
+          sb[k] = s4.x; sb[k + 1] = s4.y; sb[k + 2] = s4.z; sb[k + 3] = s4.w;
+        }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float z1 = __fmul_rn(__low2float(R[i + u]), coef), z2 = __fmul_rn(__high2float(R[i + u]), coef);
-          float k1 = __fsub_rn(__fmul_rn(z1, cc[u]), __fmul_rn(z2, ss[u]));
-          float k2 = __fadd_rn(__fmul_rn(z1, ss[u]), __fmul_rn(z2, cc[u]));
-          if (a.key_sharpen != 1.0f) {
-            k1 = __fmul_rn(k1, a.key_sharpen);
-            k2 = __fmul_rn(k2, a.key_sharpen);
+        for (int i = i0; i < i0 + AT_ROPE_BATCH; i += 8) {
+        const float* cc = cb + (i - i0);
+        const float* ss = sb + (i - i0);
+        uint32_t lo[4], hi[4];
+#pragma unroll
+        for (int u = 0; u < 8; u += 2) {
+          float k1[2], k2[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const float2 r = __half22float2(R[i + u + e]);
+            float z1, z2, m1, m2, n1, n2;
+            upk(mul2(pk(r.x, r.y), coef2), z1, z2);
+            upk(mul2(pk(z1, z2), pk(cc[u + e], cc[u + e])), m1, m2);
+            upk(mul2(pk(z1, z2), pk(ss[u + e], ss[u + e])), n1, n2);
+            u64 kk = pk(__fsub_rn(m1, n2), __fadd_rn(n1, m2));
+            if (a.key_sharpen != 1.0f) kk = mul2(kk, sh2);
+            upk(kk, k1[e], k2[e]);
           }
-          k1 = __half2float(__float2half_rn(k1));  // the fp16 key the dequantize path stores
-          k2 = __half2float(__float2half_rn(k2));
-#pragma unroll
-          for (int g = 0; g < G; ++g) s[g] = fmaf(qs[g][i + u], k1, fmaf(qs[g][i + u + 64], k2, s[g]));
+          const __half2 hl = __floats2half2_rn(k1[0], k1[1]), hh = __floats2half2_rn(k2[0], k2[1]);
+          lo[u / 2] = *reinterpret_cast<const uint32_t*>(&hl);
+          hi[u / 2] = *reinterpret_cast<const uint32_t*>(&hh);
+        }
+        const int c = i >> 3;
+        *reinterpret_cast<uint4*>(kb + tid * 128 + ((c ^ (tid & 7)) << 4)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        *reinterpret_cast<uint4*>(kb + 16384 + tid * 128 + ((c ^ (tid & 7)) << 4)) =
+            make_uint4(hi[0], hi[1], hi[2], hi[3]);
         }
       }
-      sv = __half2float(__ushort_as_half(a.v_scales[row0 + t]));
-      const uint4* src = reinterpret_cast<const uint4*>(a.v_codes + (row0 + t) * PBV);
+    } else {
 #pragma unroll
-      for (int k = 0; k < PBV / 16; ++k) reinterpret_cast<uint4*>(vrow[tid])[k] = __ldg(src + k);
+      for (int c = 0; c < 8; ++c) {
+        *reinterpret_cast<uint4*>(kb + tid * 128 + (c << 4)) = make_uint4(0u, 0u, 0u, 0u);
+        *reinterpret_cast<uint4*>(kb + 16384 + tid * 128 + (c << 4)) = make_uint4(0u, 0u, 0u, 0u);
+      }
     }
-    // tile maxima -> new running maxima (same value in every thread)
+    // ---- value t's codes -> token row tid of the MN-major value tile (zeros past the end)
+    {
+      uint32_t w[PBV / 4 + 1];
+      if (valid) {
+        const uint4* src = reinterpret_cast<const uint4*>(a.v_codes + (row0 + t) * PBV);
+#pragma unroll
+        for (int k = 0; k < PBV / 16; ++k) {
+          const uint4 u = __ldg(src + k);
+          w[4 * k] = u.x; w[4 * k + 1] = u.y; w[4 * k + 2] = u.z; w[4 * k + 3] = u.w;
+        }
+      }
+      w[PBV / 4] = 0u;
+      uint8_t* vrow = vb + (tid >> 3) * 1024 + (tid & 7) * 128;
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {  // 8 dimensions per 16-byte chunk; chunks 8..15 in the second M block
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (valid) {
+          v.x = at_code_pair<FMTV>(w, 4 * c);
+          v.y = at_code_pair<FMTV>(w, 4 * c + 1);
+          v.z = at_code_pair<FMTV>(w, 4 * c + 2);
+          v.w = at_code_pair<FMTV>(w, 4 * c + 3);
+        }
+        *reinterpret_cast<uint4*>(vrow + (c >> 3) * 16384 + (((c & 7) ^ (tid & 7)) << 4)) = v;
+      }
+    }
+    const float sv = valid ? __half2float(__ushort_as_half(a.v_scales[row0 + t])) : 0.0f;
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    // ---- S = K Q^T
+    if (tid == 0 && !err) {
+      tc_fence_after();
+#pragma unroll
+      for (int k = 0; k < kAtD / 16; ++k) {
+        const int blk = k >> 2, off = (k & 3) * 32;
+        umma_f16(tS, sw128_desc(kb + blk * 16384 + off), sw128_desc(qb + blk * 2048 + off), kIdescQK, k > 0 ? 1u : 0u);
+      }
+      umma_commit(&barS);
+    }
+    if (!mbar_wait(&barS, ph)) err = 1;
+    tc_fence_after();
+    float x[16];
+    tmem_ld16(tS + lane_off, x);
+    // ---- online softmax over the tile (base-2 logits)
+    float s[G];
 #pragma unroll
     for (int g = 0; g < G; ++g) {
+      s[g] = valid ? x[g] * qscale : -INFINITY;
       float v = s[g];
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -211,61 +343,107 @@ __global__ void __launch_bounds__(kAtTok, 3) attend_partial(const AttendArgs a) 
       alpha[g] = m[g] == -INFINITY ? 0.0f : ex2a(m[g] - mn);
       m[g] = mn;
       const float p = valid ? ex2a(s[g] - mn) : 0.0f;
-      wgt[g][tid] = p * sv;
-      s[g] = p;
+      lsum[g] = fmaf(lsum[g], alpha[g], p);
+      *reinterpret_cast<__half*>(wb + sw128_off(g, tid, 2048)) = __float2half_rn(valid ? p * sv : 0.0f);
     }
+    fence_proxy_async_smem();
+    tc_fence_before();
     __syncthreads();
-    // tile sums of p
+    // ---- O = C^T W^T (value codes, M = dimensions)
+    if (tid == 0 && !err) {
+      tc_fence_after();
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      float v = s[g];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      if (lane == 0) red[g][warp] = v;
+      for (int k = 0; k < kAtTok / 16; ++k) {
+        const int blk = k >> 2, off = (k & 3) * 32;
+        umma_f16(tO, sw128_mn_desc(vb + k * 2048, 16384, 1024), sw128_desc(wb + blk * 2048 + off), kIdescPV,
+                 k > 0 ? 1u : 0u);
+      }
+      umma_commit(&barO);
     }
-    __syncthreads();
-    const int nt = min(kAtTok, t1 - base);
+    if (!mbar_wait(&barO, ph)) err = 1;
+    tc_fence_after();
+    float o[16];
+    tmem_ld16(tO + lane_off, o);
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      l[g] = l[g] * alpha[g] + ((red[g][0] + red[g][1]) + (red[g][2] + red[g][3]));
-      acc[g] *= alpha[g];
-    }
-    // values in the code domain: thread tid owns dimension tid
-    for (int u = 0; u < nt; ++u) {
-      const float c = (float)at_code<FMTV>(vrow[u], tid);
-#pragma unroll
-      for (int g = 0; g < G; ++g) acc[g] = fmaf(wgt[g][u], c, acc[g]);
-    }
-    __syncthreads();
+    for (int g = 0; g < G; ++g) acc[g] = fmaf(acc[g], alpha[g], o[g]);
+    tc_fence_before();
+    __syncthreads();  // the tiles and TMEM columns are free for the next tile
+    if (err) break;
   }
+  // ---- per query head: running max, softmax sum (fixed-order reduction), accumulator
   const int64_t o = ((int64_t)b * a.q_heads + kh * G) * a.splits + split;
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float v = lsum[g];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    if (lane == 0) red[g][warp] = v;
+  }
+  __syncthreads();
 #pragma unroll
   for (int g = 0; g < G; ++g) {
     const int64_t og = o + (int64_t)g * a.splits;
     if (tid == 0) {
       a.ws_m[og] = m[g];
-      a.ws_l[og] = l[g];
+      a.ws_l[og] = (red[g][0] + red[g][1]) + (red[g][2] + red[g][3]);
     }
     a.ws_acc[og * kAtD + tid] = acc[g];
   }
+  if (tid == 0 && err) {
+    // a tile whose MMA was not waited for must finish before TMEM is freed
+    mbar_wait(&barS, ph, 1u << 20);
+    mbar_wait(&barO, ph, 1u << 20);
+    atomicOr(&g_attend_wait_error, 1u);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem_base, 32);
 }
+
+// Merge of the splits: split weights f_s = 2^(m_s - M) computed once per split in parallel,
+// then every dimension sums its accumulators in split order with independent loads.
+constexpr int kAtMaxSplits = 1024;
 
 __global__ void __launch_bounds__(kAtD) attend_combine(const AttendArgs a) {
   __shared__ float y[kAtD];
-  const int qh = blockIdx.x, b = blockIdx.y, j = threadIdx.x;
-  const int64_t o = ((int64_t)b * a.q_heads + qh) * a.splits;
+  __shared__ float f[kAtMaxSplits];
+  __shared__ float red[kAtD / 32];
+  const int qh = blockIdx.x, b = blockIdx.y, j = threadIdx.x, lane = j & 31, warp = j >> 5;
+  const int S = a.splits;
+  const int64_t o = ((int64_t)b * a.q_heads + qh) * S;
   float M = -INFINITY;
-  for (int s = 0; s < a.splits; ++s) M = fmaxf(M, a.ws_m[o + s]);
-  float L = 0.0f, v = 0.0f;
-  if (M != -INFINITY) {
-    for (int s = 0; s < a.splits; ++s) {
-      const float ms = a.ws_m[o + s];
-      if (ms == -INFINITY) continue;
-      const float f = ex2a(ms - M);
-      L = fmaf(a.ws_l[o + s], f, L);
-      v = fmaf(a.ws_acc[(o + s) * kAtD + j], f, v);
-    }
+  for (int s = j; s < S; s += kAtD) M = fmaxf(M, a.ws_m[o + s]);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+  if (lane == 0) red[warp] = M;
+  __syncthreads();
+  M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  __syncthreads();
+  float L = 0.0f;
+  for (int s = j; s < S; s += kAtD) {
+    const float ms = a.ws_m[o + s];
+    const float fs = (ms == -INFINITY || M == -INFINITY) ? 0.0f : ex2a(ms - M);
+    f[s] = fs;
+    L = fmaf(a.ws_l[o + s], fs, L);
   }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+  if (lane == 0) red[warp] = L;
+  __syncthreads();
+  L = (red[0] + red[1]) + (red[2] + red[3]);
+  const float* accp = a.ws_acc + o * kAtD + j;
+  float v0 = 0.0f, v1 = 0.0f, v2 = 0.0f, v3 = 0.0f;
+  int s = 0;
+  for (; s + 4 <= S; s += 4) {
+    const float x0 = accp[(int64_t)s * kAtD], x1 = accp[(int64_t)(s + 1) * kAtD];
+    const float x2 = accp[(int64_t)(s + 2) * kAtD], x3 = accp[(int64_t)(s + 3) * kAtD];
+    v0 = fmaf(x0, f[s], v0);
+    v1 = fmaf(x1, f[s + 1], v1);
+    v2 = fmaf(x2, f[s + 2], v2);
+    v3 = fmaf(x3, f[s + 3], v3);
+  }
+  for (; s < S; ++s) v0 = fmaf(accp[(int64_t)s * kAtD], f[s], v0);
+  const float v = (v0 + v1) + (v2 + v3);
   y[j] = L > 0.0f ? v / L : 0.0f;
   __syncthreads();
   // inverse Walsh-Hadamard (stride 1, 2, ... 64) across the 128 threads
@@ -279,6 +457,19 @@ __global__ void __launch_bounds__(kAtD) attend_combine(const AttendArgs a) {
   a.out[(int64_t)b * a.out_stride_b + (int64_t)qh * a.out_stride_h + j] = __float2half_rn(r);
 }
 
+cudaError_t attend_take_error(unsigned int* bits, cudaStream_t s) {
+  unsigned int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(&v, g_attend_wait_error, sizeof(v), 0, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e == cudaSuccess && v) {
+    const unsigned int zero = 0;
+    e = cudaMemcpyToSymbolAsync(g_attend_wait_error, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  }
+  *bits = v;
+  return e;
+}
+
 size_t attend_workspace_bytes(int batch, int q_heads, int splits) {
   const size_t n = (size_t)batch * q_heads * splits;
   return n * sizeof(float) * (2 + kAtD) + 3 * 256;
@@ -290,19 +481,25 @@ int attend_splits(int batch, int heads, int n_tokens) {
   const int tiles = (n_tokens + kAtTok - 1) / kAtTok;
   // one wave of attend_partial at 3 resident CTAs per SM
   const long long want = (3LL * sms + (long long)batch * heads - 1) / ((long long)batch * heads);
-  return (int)std::max(1LL, std::min<long long>(tiles, want));
+  return (int)std::max(1LL, std::min<long long>(std::min<long long>(tiles, want), kAtMaxSplits));
 }
 
 template <int FMTK, int FMTV>
 static cudaError_t attend_g(const AttendArgs& a, int G, cudaStream_t s) {
   const dim3 grid(a.splits, a.heads, a.batch);
+  cudaError_t e = cudaSuccess;
+  auto run = [&](auto kern) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, AtSmem::kBytes);
+    if (e == cudaSuccess) kern<<<grid, kAtTok, AtSmem::kBytes, s>>>(a);
+  };
   switch (G) {
-    case 1: attend_partial<FMTK, FMTV, 1><<<grid, kAtTok, 0, s>>>(a); break;
-    case 2: attend_partial<FMTK, FMTV, 2><<<grid, kAtTok, 0, s>>>(a); break;
-    case 4: attend_partial<FMTK, FMTV, 4><<<grid, kAtTok, 0, s>>>(a); break;
-    case 8: attend_partial<FMTK, FMTV, 8><<<grid, kAtTok, 0, s>>>(a); break;
+    case 1: run(attend_partial<FMTK, FMTV, 1>); break;
+    case 2: run(attend_partial<FMTK, FMTV, 2>); break;
+    case 4: run(attend_partial<FMTK, FMTV, 4>); break;
+    case 8: run(attend_partial<FMTK, FMTV, 8>); break;
     default: return cudaErrorInvalidValue;
   }
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

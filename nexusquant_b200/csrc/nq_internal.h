@@ -132,6 +132,7 @@ struct AttendArgs {
 };
 int attend_splits(int batch, int heads, int n_tokens);
 size_t attend_workspace_bytes(int batch, int q_heads, int splits);
+cudaError_t attend_take_error(unsigned int* bits, cudaStream_t s);  // read and clear its wait-error word
 cudaError_t launch_attend(const AttendArgs& a, int fmt_k, int fmt_v, void* ws, cudaStream_t s);
 
 }  // namespace nq

@@ -357,8 +357,8 @@ def score_keykey(k: torch.Tensor, obs_window: int = 32, head_range=None, per_hea
 
 def check_device_errors(device=None) -> int:
     """Synchronize the device's current stream and raise NexusQuantError (NQ_ERR_TIMEOUT) if a
-    bounded device-side wait expired since the last check (the scorer's results are then not
-    valid); clears the device's error word.  Returns 0."""
+    bounded device-side wait expired since the last check (the scorer's or the decode
+    attention's results are then not valid); clears the device's error word.  Returns 0."""
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
     bits = ctypes.c_int32(0)
     with torch.cuda.device(dev):
