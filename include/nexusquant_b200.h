@@ -342,6 +342,15 @@ nq_status_t nq_merge_centroid_accumulate(const void *const *values, int32_t n_la
                                          int32_t accumulate, float *centroid_sum, nq_stream_t stream);
 nq_status_t nq_merge_centroid_normalize(const float *centroid_sum, int32_t seq, int32_t head_dim,
                                         int32_t n_layers, float *unit_rows, nq_stream_t stream);
+/* Same result as nq_merge_nearest for head_dim 128 and rows of norm <= 1 + 1e-6 (what
+ * nq_merge_centroid_normalize writes); no counterpart in the reference.  The similarities are
+ * screened on the tensor cores (tf32, fp32 accumulation) keeping every column within 0.005 of
+ * the row maximum (more than twice the tf32 error bound for unit rows); those candidates are
+ * re-computed in the exact kernel's fp32 order, so the chosen indices are identical.  Rows that
+ * run out of candidate slots, contain NaN or are not unit rows fall back to the exact scan. */
+nq_status_t nq_merge_nearest_unit(const float *unit_rows, int32_t head_dim, const int32_t *evict_pos,
+                                  int32_t n_evict, const int32_t *kept_pos, int32_t n_kept, int32_t *nearest,
+                                  nq_stream_t stream);
 nq_status_t nq_merge_nearest(const float *unit_rows, int32_t head_dim, const int32_t *evict_pos, int32_t n_evict,
                              const int32_t *kept_pos, int32_t n_kept, int32_t *nearest, nq_stream_t stream);
 nq_status_t nq_merge_apply(const void *const *values, int32_t n_layers, int32_t dtype, int32_t heads, int32_t seq,

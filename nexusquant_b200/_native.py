@@ -106,6 +106,7 @@ _PROTOS = {
                                              c_i64, c_i32, c_vp, c_vp]),
     "nq_merge_centroid_normalize": (c_i32, [c_vp, c_i32, c_i32, c_i32, c_vp, c_vp]),
     "nq_merge_nearest": (c_i32, [c_vp, c_i32, c_vp, c_i32, c_vp, c_i32, c_vp, c_vp]),
+    "nq_merge_nearest_unit": (c_i32, [c_vp, c_i32, c_vp, c_i32, c_vp, c_i32, c_vp, c_vp]),
     "nq_unpack_codes": (c_i32, [c_vp, c_i64, c_i32, c_i32, c_vp, c_vp]),
     "nq_pack_nibbles": (c_i32, [c_vp, c_i64, c_i32, c_vp, c_vp]),
     "nq_unpack_nibbles": (c_i32, [c_vp, c_i64, c_i32, c_vp, c_vp]),

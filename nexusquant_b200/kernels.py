@@ -444,6 +444,22 @@ def gather_rows(x: torch.Tensor, kept_idx: Optional[torch.Tensor], n_kept: int,
     return out
 
 
+def merge_nearest(unit: torch.Tensor, evict_pos: torch.Tensor, kept_pos: torch.Tensor, *,
+                  tensor_cores: bool = True) -> torch.Tensor:
+    """nearest[i] = argmax_j unit[evict_pos[i]] . unit[kept_pos[j]] (first j on ties) for fp32 unit
+    rows [seq, d]: nq_merge_nearest_unit (d = 128, tensor-core screening with an exact
+    re-check) or nq_merge_nearest (the exact fp32 kernel)."""
+    _require_cuda(unit)
+    unit = unit.contiguous()
+    ev = evict_pos.to(device=unit.device, dtype=torch.int32).contiguous()
+    kp = kept_pos.to(device=unit.device, dtype=torch.int32).contiguous()
+    out = torch.empty(ev.numel(), dtype=torch.int32, device=unit.device)
+    fn = "nq_merge_nearest_unit" if tensor_cores else "nq_merge_nearest"
+    N.call(fn, unit.data_ptr(), unit.shape[1], ev.data_ptr(), ev.numel(), kp.data_ptr(), kp.numel(), out.data_ptr(),
+           _stream(unit.device))
+    return out
+
+
 def merge_evicted_values(vs: Sequence[torch.Tensor], keep_mask: torch.Tensor, importance: torch.Tensor,
                          nearest_out: Optional[List[torch.Tensor]] = None) -> None:
     """Merge eviction, in place on ``vs`` (nexusquant/pipeline.py:961-1048): for every batch
@@ -495,8 +511,9 @@ def merge_evicted_values(vs: Sequence[torch.Tensor], keep_mask: torch.Tensor, im
             first = False
         N.call("nq_merge_centroid_normalize", acc.data_ptr(), T, d, len(layers), acc.data_ptr(), stream)
         nearest = torch.empty(n_e, dtype=torch.int32, device=dev)
-        N.call("nq_merge_nearest", acc.data_ptr(), d, evict.data_ptr(), n_e, kept.data_ptr(), n_k,
-               nearest.data_ptr(), stream)
+        # unit rows at head_dim 128: tensor-core screening + exact re-check (same choices)
+        N.call("nq_merge_nearest_unit" if d == 128 else "nq_merge_nearest", acc.data_ptr(), d, evict.data_ptr(),
+               n_e, kept.data_ptr(), n_k, nearest.data_ptr(), stream)
         order = torch.argsort(nearest, stable=True)
         seg_evicted = evict[order].contiguous()
         seg_start = torch.zeros(n_k + 1, dtype=torch.int32, device=dev)

@@ -183,3 +183,52 @@ def test_evict_with_merge_matches_reference_pipeline(mg):
     # the caller's tensors are not modified (the reference merges into clones)
     for a, o in zip(inputs, orig):
         assert torch.equal(a, o)
+
+
+def _unit_rows(seq, seed, d=128, structured=False):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(seq, d, generator=g)
+    if structured:  # correlated rows: a few directions plus noise, like averaged value rows
+        base = torch.randn(8, d, generator=g)
+        x = base[torch.randint(0, 8, (seq,), generator=g)] + 0.3 * x
+    return torch.nn.functional.normalize(x, dim=1)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("seed,seq,structured", [(0, 5000, False), (1, 20011, True), (2, 777, True), (3, 300, False)])
+def test_nearest_unit_equals_exact_kernel(seed, seq, structured):
+    """Tensor-core screening + exact re-check picks exactly the exact kernel's indices."""
+    from nexusquant_b200 import kernels as K
+    u = _unit_rows(seq, seed, structured=structured).to(DEV)
+    g = torch.Generator().manual_seed(100 + seed)
+    perm = torch.randperm(seq, generator=g)
+    nk = max(1, seq // 5 + seed)
+    kept, ev = perm[:nk].sort().values, perm[nk:].sort().values
+    a = K.merge_nearest(u, ev, kept, tensor_cores=True)
+    b = K.merge_nearest(u, ev, kept, tensor_cores=False)
+    assert torch.equal(a, b)
+
+
+@pytest.mark.gpu
+def test_nearest_unit_ties_overflow_nan_and_non_unit_rows():
+    """Exact ties (first index wins), more near-ties than candidate slots (exact fallback),
+    a NaN evicted row (index 0, as torch.argmax) and a non-unit evicted row."""
+    from nexusquant_b200 import kernels as K
+    seq = 3000
+    u = _unit_rows(seq, 7)
+    target = u[0].clone()
+    g = torch.Generator().manual_seed(11)
+    for i in range(1, 41):  # 40 kept rows within ~1e-6 of the first evicted row's direction
+        u[100 + i] = torch.nn.functional.normalize(target + 1e-6 * torch.randn(128, generator=g), dim=0)
+    u[200] = target
+    u[201] = target                      # exact tie between kept rows 200 and 201
+    u[5] = float("nan")                  # NaN evicted row
+    u[6] = 2.0 * u[6]                    # not a unit row
+    u = u.to(DEV)
+    ev = torch.tensor([0, 5, 6] + list(range(1000, 1400)))
+    kept = torch.tensor(list(range(100, 142)) + [200, 201] + list(range(2000, 2600)))
+    a = K.merge_nearest(u, ev, kept, tensor_cores=True)
+    b = K.merge_nearest(u, ev, kept, tensor_cores=False)
+    bad = (a != b).nonzero().flatten().tolist()
+    assert not bad, (bad[:8], a[bad[:8]].tolist(), b[bad[:8]].tolist())
+    assert int(a[1]) == 0
