@@ -244,8 +244,11 @@ __device__ __forceinline__ void decompress_vector(const DecompressArgs& args, co
 
 // KEY: this launch covers the key rows (true) or the value rows (false) of every layer; one
 // half per kernel keeps each kernel's code (three packing formats) small for the i-cache.
+// 5 CTAs per SM for keys (93 registers) and 6 for values (80; 5 at d = 96), without spills:
+// the kernel is latency-bound on its code loads, and the extra warps hide it (4 CTAs: 0.625
+// of the measured HBM peak on config 3, 5: 0.679).
 template <int D, int DP, bool V8, bool KEY>
-__global__ void __launch_bounds__(kCompressThreads, 4) decompress_kernel(const DecompressArgs args) {
+__global__ void __launch_bounds__(kCompressThreads, (KEY || D == 96) ? 5 : 6) decompress_kernel(const DecompressArgs args) {
   extern __shared__ __align__(16) uint8_t rope_smem[];
   const int HG = args.head_group;
   const int TOK = kCompressThreads / HG;
