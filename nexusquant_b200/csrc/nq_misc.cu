@@ -4,24 +4,21 @@
 
 namespace nq {
 
-// out[b, h, j, :] = fp16(in[b, h, kept_idx[b, j], :]); one thread per 8 elements.
+// out[b, h, j, :] = fp16(in[b, h, kept_idx[b, j], :]); one thread per 8 elements, grid rows
+// walking the (b, h) pairs so the index arithmetic is 32-bit.
 // Replaces the protected-layer branch of NexusQuantEvict(Truncate).compress
 // (nexusquant/pipeline.py:1206-1210, :1363-1368).
 template <typename T>
-__global__ void gather_rows_kernel(const T* in, int batch, int heads, int head_dim, int64_t isb, int64_t ish,
-                                   int64_t ist, const int32_t* kept_idx, const int32_t* kept_count, int n_kept,
-                                   __half* out, int64_t osb, int64_t osh, int64_t ost) {
+__global__ void gather_rows_kernel(const T* in, int batch, int heads, int head_dim, int64_t isb, int64_t ish, int64_t ist,
+                                   const int32_t* kept_idx, const int32_t* kept_count, int n_kept, __half* out,
+                                   int64_t osb, int64_t osh, int64_t ost) {
   const int chunks = head_dim / 8;
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int64_t total = (int64_t)batch * heads * n_kept * chunks;
-  if (i >= total) return;
-  const int c = (int)(i % chunks);
-  int64_t r = i / chunks;
-  const int j = (int)(r % n_kept); r /= n_kept;
-  const int h = (int)(r % heads);
-  const int b = (int)(r / heads);
-  const int cnt = kept_count ? kept_count[b] : n_kept;
-  if (j >= cnt) return;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  const int j = i / chunks, c = i - j * chunks;
+  for (int bh = blockIdx.y; bh < batch * heads; bh += gridDim.y) {
+  const int b = bh / heads, h = bh - b * heads;
+  const int cnt = kept_count ? min(kept_count[b], n_kept) : n_kept;
+  if (j >= cnt) continue;
   const int src = kept_idx ? kept_idx[(int64_t)b * n_kept + j] : j;
   const T* p = in + b * isb + h * ish + (int64_t)src * ist + 8 * c;
   float v[8];
@@ -34,28 +31,31 @@ __global__ void gather_rows_kernel(const T* in, int batch, int heads, int head_d
   u.z = *reinterpret_cast<uint32_t*>(&h2);
   u.w = *reinterpret_cast<uint32_t*>(&h3);
   *reinterpret_cast<uint4*>(out + b * osb + h * osh + (int64_t)j * ost + 8 * c) = u;
+  }
 }
 
 cudaError_t launch_gather_rows(const void* in, int dtype, int batch, int heads, int head_dim, int64_t isb,
                                int64_t ish, int64_t ist, const int32_t* kept_idx, const int32_t* kept_count,
                                int n_kept, uint16_t* out, int64_t osb, int64_t osh, int64_t ost, cudaStream_t s) {
-  const int64_t total = (int64_t)batch * heads * n_kept * (head_dim / 8);
-  if (total == 0) return cudaSuccess;
-  const unsigned blocks = (unsigned)((total + 255) / 256);
+  const int64_t per_head = (int64_t)n_kept * (head_dim / 8);
+  if (per_head == 0 || batch == 0 || heads == 0) return cudaSuccess;
+  if (per_head > 0x7fffffffLL - 256 || (int64_t)batch * heads > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+  const int64_t bh = (int64_t)batch * heads;
+  const dim3 grid((unsigned)((per_head + 255) / 256), (unsigned)(bh < 65535 ? bh : 65535));
   __half* o = reinterpret_cast<__half*>(out);
   switch (dtype) {
     case 0:
-      gather_rows_kernel<__half><<<blocks, 256, 0, s>>>(static_cast<const __half*>(in), batch, heads, head_dim, isb,
-                                                         ish, ist, kept_idx, kept_count, n_kept, o, osb, osh, ost);
+      gather_rows_kernel<__half><<<grid, 256, 0, s>>>(static_cast<const __half*>(in), batch, heads, head_dim, isb, ish, ist,
+                                                      kept_idx, kept_count, n_kept, o, osb, osh, ost);
       break;
     case 1:
-      gather_rows_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(in), batch, heads,
-                                                                head_dim, isb, ish, ist, kept_idx, kept_count,
-                                                                n_kept, o, osb, osh, ost);
+      gather_rows_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(in), batch, heads, head_dim,
+                                                             isb, ish, ist, kept_idx, kept_count, n_kept, o, osb,
+                                                             osh, ost);
       break;
     case 2:
-      gather_rows_kernel<float><<<blocks, 256, 0, s>>>(static_cast<const float*>(in), batch, heads, head_dim, isb,
-                                                        ish, ist, kept_idx, kept_count, n_kept, o, osb, osh, ost);
+      gather_rows_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float*>(in), batch, heads, head_dim, isb, ish, ist,
+                                                     kept_idx, kept_count, n_kept, o, osb, osh, ost);
       break;
     default:
       return cudaErrorInvalidValue;
