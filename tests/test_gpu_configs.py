@@ -129,3 +129,15 @@ def test_config2_real_scorer_layer_parity(orc):
         qs.append(syn.cpu_queries(cfg, l))
     kept, kidx, kcnt, cap = _keep_set(orc, cfg, ks[0], qs, ks)
     _layer_parity(orc, cfg, ks[1], vs[1], kept, kidx, kcnt, cap)
+
+
+@pytest.mark.parametrize("heads", [1, 2, 4])
+def test_config4_head_slice_parity(orc, heads):
+    """The per-rank shapes of config 4's head-sharded runs at 8, 4 and 2 GPUs (1, 2 and 4 KV
+    heads per rank: head groups of 1, 2 and 4 in the compress and dequantize tiles), RoPE base
+    5e5, K2V2 after the key-key keep set, at T = 16384 so the oracle finishes in seconds."""
+    cfg = syn.CacheConfig("cfg4_slice", 2, 1, heads, 16384, 128, rope_base=500000.0, key_bits=2, value_bits=2,
+                          eviction_rate=0.8)
+    k, v = syn.cpu_layer(cfg, 0)
+    kept, kidx, kcnt, cap = _keep_set(orc, cfg, k)
+    _layer_parity(orc, cfg, k, v, kept, kidx, kcnt, cap)
