@@ -22,7 +22,9 @@ needed between steps.
 The same JSON line carries the kernel-only compress and dequantize rooflines of this
 configuration and (on one GPU) of configs 1-3, the end-to-end number through
 ``NexusQuantEvict(layout="compressed")`` on a cache in pinned host memory, the CPU
-baseline, and the entropy-coded size (zstd host post-step, outside the timed region).
+baseline, the entropy-coded size (zstd and rANS host post-steps, outside the timed region),
+and (`extras`, one GPU) the device times of the tensor-core decode attention and merge
+survivor search on the step's own data.
 """
 from __future__ import annotations
 
@@ -513,6 +515,56 @@ def entropy_leg(cache, cfg, max_tokens: int = 2048) -> dict:
     return r
 
 
+def extras_leg(sh, steps: int) -> dict:
+    """Device times of the secondary tensor-core kernels on this step's own data (rank 0, one
+    GPU, outside the headline): decode attention over the first quantized layer's codes (8
+    query heads per KV head, CUDA-graph replay), and merge eviction's nearest-survivor search on
+    unit centroids of 8 value layers, tensor-core screening against the exact fp32 kernel."""
+    cfg, dev = sh.cfg, sh.dev
+    out = {}
+    if sh.quant and cfg.head_dim == 128:
+        lc = sh.codes[0]
+        b, hl = cfg.batch, sh.hl
+        g = torch.Generator(device=dev).manual_seed(0)
+        q = (torch.randn(b, 8 * hl, 128, device=dev, generator=g) * 0.3).half()
+        outq = torch.empty_like(q)
+
+        def att():
+            K.attend_compressed(q, lc, sh.kept_idx, count=sh.kept_count, rope_base=cfg.rope_base,
+                                rope_rows=cfg.seq, out=outq)
+        att()
+        s2 = torch.cuda.Stream()
+        s2.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s2):
+            att()
+        torch.cuda.current_stream().wait_stream(s2)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(steps):
+                att()
+        us = timed(graph.replay, 1, 3, 1) / steps * 1e3
+        nbytes = sum(t.numel() * t.element_size() for t in (lc.k_codes, lc.v_codes, lc.k_scales, lc.v_scales))
+        out["attend_compressed"] = {"us": round(us, 2), "kv_heads": hl, "q_heads": 8 * hl, "tokens": sh.cap,
+                                    "gbs_of_compressed_bytes": round(nbytes / us / 1e3, 1),
+                                    "kernel": "attend_partial (tcgen05 S = K Q^T, O = C^T W^T) + attend_combine"}
+    layers = sh.quant[:8]
+    if cfg.eviction_rate > 0 and len(layers) == 8 and cfg.head_dim == 128 and cfg.batch == 1:
+        cen = sum(sh.V[l][0].float().mean(0) for l in layers) / 8.0
+        unit = torch.nn.functional.normalize(cen, dim=1).contiguous()
+        kept_mask = torch.zeros(cfg.seq, dtype=torch.bool, device=dev)
+        kept = sh.kept_idx[0, :int(sh.kept_count[0])].long()
+        kept_mask[kept] = True
+        ev = torch.nonzero(~kept_mask).flatten()
+        res = {}
+        for tc in (True, False):
+            r = K.merge_nearest(unit, ev, kept, tensor_cores=tc)
+            res[tc] = (timed(lambda: K.merge_nearest(unit, ev, kept, tensor_cores=tc), 3, 3, 1) / 3, r)
+        out["merge_nearest"] = {"ms_tensor_cores": round(res[True][0], 3), "ms_exact_fp32": round(res[False][0], 3),
+                                "evicted": int(ev.numel()), "kept": int(kept.numel()),
+                                "same_indices": bool(torch.equal(res[True][1], res[False][1]))}
+    return out
+
+
 # ------------------------------------------------------------------- reference
 def run_reference(args, cfg, rank, world):
     if rank != 0:
@@ -689,6 +741,13 @@ def main():
     except (OSError, KeyError, ValueError):
         pass
 
+    extras = None
+    if rank == 0 and world == 1 and not args.profile and not args.no_per_config:
+        try:
+            extras = extras_leg(sh, args.steps)
+        except Exception as ex:  # reported, never fatal: outside the headline
+            extras = {"error": f"{type(ex).__name__}: {ex}"}
+
     e2e, e2e_err, host_cache = None, "disabled", None
     if not args.no_e2e and not args.profile:
         with GpuLocalCpus(local):
@@ -728,6 +787,7 @@ def main():
                          "frac_of_spec_8tbs": round(kr["dequant"]["achieved"] / 8000.0, 4),
                          "launch_ms": kr["dequant"]["launch_ms"], "algo_bytes": algo} if kr else None),
             "per_config": per_cfg,
+            "extras": extras,
             "entropy": ent,
             "cpu_baseline": cpu,
             "e2e": e2e if e2e is not None else {"value": None, "unit": "GB/s", "error": e2e_err},
