@@ -7,15 +7,16 @@
 // heads (q head g*G .. g*G+G-1 reads KV head g; G = 1 is the reference's case).
 //
 // Split-K over tokens, two kernels:
-//  * attend_partial: CTA = (token split, KV head, batch), 128 threads, both contractions on
+//  * attend_partial: CTA = (token split, KV head, batch), 256 threads, both contractions on
 //    the 5th-generation tensor cores (tcgen05.mma kind::f16, fp32 accumulators in TMEM).
 //    Per tile of 128 tokens:
-//      - thread t decodes key t in registers (unpack -> exact half2 butterfly -> scale ->
-//        RoPE -> sharpen -> fp16, the dequantize kernel's arithmetic) into a K-major,
-//        128-byte-swizzled shared tile, and converts value t's codes (small integers, exact
-//        in fp16) into an MN-major swizzled tile;
+//      - the two threads of token t decode its key in registers, half of the coordinate
+//        pairs each (unpack -> exact half2 butterfly, one stage across the pair by shuffle ->
+//        scale -> RoPE -> sharpen -> fp16, the dequantize kernel's arithmetic) into a K-major,
+//        128-byte-swizzled shared tile, and convert half of value t's codes each (small
+//        integers, exact in fp16) into an MN-major swizzled tile;
 //      - one thread issues S = K Q^T (M = 128 tokens, N = 16 >= G query heads, K = 128);
-//        thread t reads its token's logits back from TMEM lane t;
+//        thread t of warps 0-3 reads token t's logits back from TMEM lane t;
 //      - online softmax over the tile; the weights p_t * s_t (value scale) go to shared
 //        memory as fp16;
 //      - one thread issues O = C^T W^T (M = 128 dimensions, N = 16, K = 128 tokens): values
@@ -36,7 +37,7 @@ namespace nq {
 
 namespace {
 
-constexpr int kAtTok = 128;  // tokens per tile = threads per CTA
+constexpr int kAtTok = 128;  // tokens per tile = TMEM lanes
 constexpr int kAtD = 128;    // head_dim = d_p
 constexpr float kAtLog2e = 1.4426950408889634f;
 
@@ -156,13 +157,73 @@ __device__ __forceinline__ uint32_t at_code_pair(const uint32_t* w, int p) {
   }
 }
 
-#ifndef AT_ROPE_BATCH
-#define AT_ROPE_BATCH 8  // RoPE values (cos and sin) fetched per batch in the key decode
-#endif
+// Codes of coordinates {q, q + 64} for the 32 pairs q in [32 h, 32 h + 32) of a packed row, as
+// half2 integers (R[q - 32 h]): the half of the key that thread h of a token's pair decodes.
+template <int FMT>
+__device__ __forceinline__ void at_unpack_half(const uint8_t* p, int h, bool valid, __half2 (&R)[32]) {
+  if constexpr (FMT == 0) {
+    // dims [32h, 32h + 32): bytes [16h, 16h + 16); dims + 64: bytes [32 + 16h, 48 + 16h)
+    uint32_t wl[4] = {0u, 0u, 0u, 0u}, wh[4] = {0u, 0u, 0u, 0u};
+    if (valid) {
+      const uint4 a = __ldg(reinterpret_cast<const uint4*>(p + 16 * h));
+      const uint4 b = __ldg(reinterpret_cast<const uint4*>(p + 32 + 16 * h));
+      wl[0] = a.x; wl[1] = a.y; wl[2] = a.z; wl[3] = a.w;
+      wh[0] = b.x; wh[1] = b.y; wh[2] = b.z; wh[3] = b.w;
+    }
+#pragma unroll
+    for (int q = 0; q < 32; q += 2) {
+      const int m = q >> 3, byte = (q & 7) >> 1;
+      const uint32_t u = __byte_perm(wl[m], wh[m], (uint32_t)((4 + byte) << 8 | byte));
+      R[q] = __hadd2(ah2_bits((u & 0x000F000Fu) | 0x64006400u), ah2c(-1032.0f));
+      R[q + 1] = __hfma2(ah2_bits((u & 0x00F000F0u) | 0x64006400u), ah2c(1.0f / 16.0f), ah2c(-72.0f));
+    }
+  } else if constexpr (FMT == 1) {
+    // dims [32h, 32h + 32): bits [160h, 160h + 160) = bytes [20h, 20h + 20); dims + 64: + 40 bytes
+    uint32_t wl[6] = {0u, 0u, 0u, 0u, 0u, 0u}, wh[6] = {0u, 0u, 0u, 0u, 0u, 0u};
+    if (valid) {
+      const uint32_t* pl = reinterpret_cast<const uint32_t*>(p + 20 * h);
+      const uint32_t* ph = reinterpret_cast<const uint32_t*>(p + 40 + 20 * h);
+#pragma unroll
+      for (int k = 0; k < 5; ++k) { wl[k] = __ldg(pl + k); wh[k] = __ldg(ph + k); }
+    }
+#pragma unroll
+    for (int q = 0; q < 32; ++q) {
+      const int bit = 5 * q, k = bit >> 5, s = bit & 31;
+      const uint32_t lo = __funnelshift_r(wl[k], wl[k + 1], s), hi = __funnelshift_r(wh[k], wh[k + 1], s);
+      const uint32_t u = __byte_perm(lo, hi, 0x5410u);
+      R[q] = __hadd2(ah2_bits((u & 0x001F001Fu) | 0x64006400u), ah2c(-1032.0f));
+    }
+  } else {
+    // dims [32h, 32h + 32): bytes [32h, 32h + 32); dims + 64: bytes [64 + 32h, 96 + 32h)
+    uint32_t wl[8], wh[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) { wl[k] = 0u; wh[k] = 0u; }
+    if (valid) {
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const uint4 a = __ldg(reinterpret_cast<const uint4*>(p + 32 * h) + k);
+        const uint4 b = __ldg(reinterpret_cast<const uint4*>(p + 64 + 32 * h) + k);
+        wl[4 * k] = a.x; wl[4 * k + 1] = a.y; wl[4 * k + 2] = a.z; wl[4 * k + 3] = a.w;
+        wh[4 * k] = b.x; wh[4 * k + 1] = b.y; wh[4 * k + 2] = b.z; wh[4 * k + 3] = b.w;
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 32; ++q) {
+      const int m = q >> 2, byte = q & 3;
+      const uint32_t u = __byte_perm(wl[m], wh[m], (uint32_t)((4 + byte) << 8 | byte));
+      R[q] = __hadd2(ah2_bits((u & 0x00FF00FFu) ^ 0x64806480u), ah2c(-1152.0f));
+    }
+  }
+}
 
-// 3 CTAs per SM (74 KB of shared memory each), one wave (attend_splits).
+// 256 threads: two per token for the decode (thread h of the pair takes pairs [32h, 32h + 32)
+// of the key and dimensions [64h, 64h + 64) of the value); warps 0-3 (one thread per TMEM lane)
+// run the softmax and the accumulator.  2 CTAs per SM (74 KB of shared memory each), one wave
+// (attend_splits).
+constexpr int kAtThreads = 256;
+
 template <int FMTK, int FMTV, int G>
-__global__ void __launch_bounds__(kAtTok, 3) attend_partial(const AttendArgs a) {
+__global__ void __launch_bounds__(kAtThreads, 2) attend_partial(const AttendArgs a) {
   constexpr int PBV = at_pb<FMTV>();
   extern __shared__ uint8_t at_smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(at_smem_raw) + 1023) & ~uintptr_t(1023));
@@ -176,12 +237,14 @@ __global__ void __launch_bounds__(kAtTok, 3) attend_partial(const AttendArgs a) 
   __shared__ int err;
   const int split = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tok = tid >> 1, hh = tid & 1;  // decode: token of the tile, half
+  const bool smx = warp < 4;               // softmax / accumulator thread: TMEM lane tid
   const int count = a.count ? min(a.count[b], a.n_tokens) : a.n_tokens;
   const int t0 = split * a.tokens_per_split, t1 = min(count, t0 + a.tokens_per_split);
   const float qscale = a.scale * kAtLog2e;
 
   // queries (fp16, exact) and the zero rows G..15 of the query and weight operands
-  for (int e = tid; e < (AtSmem::kW + 4096 - AtSmem::kQ) / 16; e += kAtTok)
+  for (int e = tid; e < (AtSmem::kW + 4096 - AtSmem::kQ) / 16; e += kAtThreads)
     reinterpret_cast<uint4*>(qb)[e] = make_uint4(0u, 0u, 0u, 0u);
   if (tid == 0) {
     mbar_init(&barS, 1);
@@ -191,7 +254,7 @@ __global__ void __launch_bounds__(kAtTok, 3) attend_partial(const AttendArgs a) 
   }
   if (warp == 0) tmem_alloc(&tmem_base, 32);
   __syncthreads();
-  for (int e = tid; e < G * kAtD; e += kAtTok) {
+  for (int e = tid; e < G * kAtD; e += kAtThreads) {
     const int g = e / kAtD, j = e % kAtD;
     *reinterpret_cast<__half*>(qb + sw128_off(g, j, 2048)) =
         a.q[(int64_t)b * a.q_stride_b + (int64_t)(kh * G + g) * a.q_stride_h + j];
@@ -200,7 +263,7 @@ __global__ void __launch_bounds__(kAtTok, 3) attend_partial(const AttendArgs a) 
   __syncthreads();
   tc_fence_after();
   const uint32_t tS = tmem_base, tO = tmem_base + 16;
-  const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+  const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
   constexpr uint32_t kIdescQK = f16_idesc(0, 128, AtSmem::kN);
   constexpr uint32_t kIdescPV = f16_idesc(0, 128, AtSmem::kN) | (1u << 15);  // A (value codes) MN-major
 
@@ -209,104 +272,116 @@ __global__ void __launch_bounds__(kAtTok, 3) attend_partial(const AttendArgs a) 
   for (int g = 0; g < G; ++g) { m[g] = -INFINITY; lsum[g] = 0.0f; acc[g] = 0.0f; }
   const int64_t row0 = ((int64_t)b * a.heads + kh) * a.n_tokens;
   const float coef_h = 0.5f * hadamard_entry(kAtD);
+  const __half2 sg = hh ? ah2c(-1.0f) : ah2c(1.0f);
   uint32_t ph = 0;
   for (int base = t0; base < t1; base += kAtTok, ph ^= 1u) {
-    const int t = base + tid;
-    const bool valid = t < t1;
-    // ---- key t -> row tid of the key tile (fp16, the dequantize kernel's values)
-    if (valid) {
-      __half2 R[64];
-      at_unpack<FMTK>(a.k_codes + (row0 + t) * at_pb<FMTK>(), R);
+    const int t = base + tok;
+    const bool valid = t < t1;  // shared by both threads of the pair: the shuffle below is uniform
+    // ---- key t, pairs [32 hh, 32 hh + 32) -> row tok of the key tile
+    {
+      __half2 R[32];
+      at_unpack_half<FMTK>(a.k_codes + (row0 + (valid ? t : t0)) * at_pb<FMTK>(), hh, valid, R);
 #pragma unroll
-      for (int st = 1; st < 64; st <<= 1)
+      for (int st = 1; st < 32; st <<= 1)
 #pragma unroll
-        for (int q = 0; q < 64; ++q)
+        for (int q = 0; q < 32; ++q)
           if ((q & st) == 0) {
             const __half2 x = R[q], y = R[q + st];
             R[q] = __hadd2(x, y);
             R[q + st] = __hsub2(x, y);
           }
+      // stride 32 crosses the pair: lower thread x + y, upper thread x - y (x = lower's value)
+#pragma unroll
+      for (int q = 0; q < 32; ++q) {
+        const uint32_t mine = *reinterpret_cast<const uint32_t*>(&R[q]);
+        const uint32_t o = __shfl_xor_sync(0xffffffffu, mine, 1);
+        R[q] = __hfma2(R[q], sg, ah2_bits(o));
+      }
       const __half2 pm = __floats2half2_rn(1.0f, -1.0f);
 #pragma unroll
-      for (int q = 0; q < 64; ++q) R[q] = __hfma2(__high2half2(R[q]), pm, __low2half2(R[q]));
-      const float coef = __fmul_rn(__half2float(__ushort_as_half(a.k_scales[row0 + t])), coef_h);
-      const int pos = min(max(a.positions[(int64_t)b * a.n_tokens + t], 0), a.rope_rows - 1);
-      const float* cs = a.rope_cos + (int64_t)pos * (kAtD / 2);
-      const float* sn = a.rope_sin + (int64_t)pos * (kAtD / 2);
-      const u64 coef2 = pk(coef, coef), sh2 = pk(a.key_sharpen, a.key_sharpen);
+      for (int q = 0; q < 32; ++q) R[q] = __hfma2(__high2half2(R[q]), pm, __low2half2(R[q]));
+      if (valid) {
+        const float coef = __fmul_rn(__half2float(__ushort_as_half(a.k_scales[row0 + t])), coef_h);
+        const int pos = min(max(a.positions[(int64_t)b * a.n_tokens + t], 0), a.rope_rows - 1);
+        const float* cs = a.rope_cos + (int64_t)pos * (kAtD / 2) + 32 * hh;
+        const float* sn = a.rope_sin + (int64_t)pos * (kAtD / 2) + 32 * hh;
+        const u64 coef2 = pk(coef, coef), sh2 = pk(a.key_sharpen, a.key_sharpen);
 #pragma unroll
-      for (int i0 = 0; i0 < 64; i0 += AT_ROPE_BATCH) {
-        // one batch of RoPE rows in flight at a time
-        float cb[AT_ROPE_BATCH], sb[AT_ROPE_BATCH];
+        for (int i = 0; i < 32; i += 8) {
+          const float4 c0 = __ldg(reinterpret_cast<const float4*>(cs + i));
+          const float4 c1 = __ldg(reinterpret_cast<const float4*>(cs + i + 4));
+          const float4 s0 = __ldg(reinterpret_cast<const float4*>(sn + i));
+          const float4 s1 = __ldg(reinterpret_cast<const float4*>(sn + i + 4));
+          const float cc[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+          const float ss[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+          uint32_t lo[4], hi[4];
 #pragma unroll
-        for (int k = 0; k < AT_ROPE_BATCH; k += 4) {
-          const float4 c4 = __ldg(reinterpret_cast<const float4*>(cs + i0 + k));
-          const float4 s4 = __ldg(reinterpret_cast<const float4*>(sn + i0 + k));
-          cb[k] = c4.x; cb[k + 1] = c4.y; cb[k + 2] = c4.z; cb[k + 3] = c4.w;
-          sb[k] = s4.x; sb[k + 1] = s4.y; sb[k + 2] = s4.z; sb[k + 3] = s4.w;
-        }
+          for (int u = 0; u < 8; u += 2) {
+            float k1[2], k2[2];
 #pragma unroll
-        for (int i = i0; i < i0 + AT_ROPE_BATCH; i += 8) {
-        const float* cc = cb + (i - i0);
-        const float* ss = sb + (i - i0);
-        uint32_t lo[4], hi[4];
-#pragma unroll
-        for (int u = 0; u < 8; u += 2) {
-          float k1[2], k2[2];
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const float2 r = __half22float2(R[i + u + e]);
-            float z1, z2, m1, m2, n1, n2;
-            upk(mul2(pk(r.x, r.y), coef2), z1, z2);
-            upk(mul2(pk(z1, z2), pk(cc[u + e], cc[u + e])), m1, m2);
-            upk(mul2(pk(z1, z2), pk(ss[u + e], ss[u + e])), n1, n2);
-            u64 kk = pk(__fsub_rn(m1, n2), __fadd_rn(n1, m2));
-            if (a.key_sharpen != 1.0f) kk = mul2(kk, sh2);
-            upk(kk, k1[e], k2[e]);
+            for (int e = 0; e < 2; ++e) {
+              const float2 r = __half22float2(R[i + u + e]);
+              float z1, z2, m1, m2, n1, n2;
+              upk(mul2(pk(r.x, r.y), coef2), z1, z2);
+              upk(mul2(pk(z1, z2), pk(cc[u + e], cc[u + e])), m1, m2);
+              upk(mul2(pk(z1, z2), pk(ss[u + e], ss[u + e])), n1, n2);
+              u64 kk = pk(__fsub_rn(m1, n2), __fadd_rn(n1, m2));
+              if (a.key_sharpen != 1.0f) kk = mul2(kk, sh2);
+              upk(kk, k1[e], k2[e]);
+            }
+            const __half2 hl = __floats2half2_rn(k1[0], k1[1]), hv = __floats2half2_rn(k2[0], k2[1]);
+            lo[u / 2] = *reinterpret_cast<const uint32_t*>(&hl);
+            hi[u / 2] = *reinterpret_cast<const uint32_t*>(&hv);
           }
-          const __half2 hl = __floats2half2_rn(k1[0], k1[1]), hh = __floats2half2_rn(k2[0], k2[1]);
-          lo[u / 2] = *reinterpret_cast<const uint32_t*>(&hl);
-          hi[u / 2] = *reinterpret_cast<const uint32_t*>(&hh);
+          const int c = 4 * hh + (i >> 3);  // 16-byte chunk of dimensions 32 hh + i ..
+          *reinterpret_cast<uint4*>(kb + tok * 128 + ((c ^ (tok & 7)) << 4)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+          *reinterpret_cast<uint4*>(kb + 16384 + tok * 128 + ((c ^ (tok & 7)) << 4)) =
+              make_uint4(hi[0], hi[1], hi[2], hi[3]);
         }
-        const int c = i >> 3;
-        *reinterpret_cast<uint4*>(kb + tid * 128 + ((c ^ (tid & 7)) << 4)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-        *reinterpret_cast<uint4*>(kb + 16384 + tid * 128 + ((c ^ (tid & 7)) << 4)) =
-            make_uint4(hi[0], hi[1], hi[2], hi[3]);
-        }
-      }
-    } else {
+      } else {
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        *reinterpret_cast<uint4*>(kb + tid * 128 + (c << 4)) = make_uint4(0u, 0u, 0u, 0u);
-        *reinterpret_cast<uint4*>(kb + 16384 + tid * 128 + (c << 4)) = make_uint4(0u, 0u, 0u, 0u);
+        for (int c = 4 * hh; c < 4 * hh + 4; ++c) {
+          *reinterpret_cast<uint4*>(kb + tok * 128 + (c << 4)) = make_uint4(0u, 0u, 0u, 0u);
+          *reinterpret_cast<uint4*>(kb + 16384 + tok * 128 + (c << 4)) = make_uint4(0u, 0u, 0u, 0u);
+        }
       }
     }
-    // ---- value t's codes -> token row tid of the MN-major value tile (zeros past the end)
+    // ---- value t's codes, dimensions [64 hh, 64 hh + 64) -> M block hh of the value tile
     {
-      uint32_t w[PBV / 4 + 1];
-      if (valid) {
-        const uint4* src = reinterpret_cast<const uint4*>(a.v_codes + (row0 + t) * PBV);
+      // this half's codes: dims [64 hh, 64 hh + 64) = bytes [PBV/2 hh, PBV/2 (hh + 1)) (local words)
+      constexpr int HW = PBV / 8;  // words per half row
+      uint32_t w[HW + 1];
 #pragma unroll
-        for (int k = 0; k < PBV / 16; ++k) {
-          const uint4 u = __ldg(src + k);
-          w[4 * k] = u.x; w[4 * k + 1] = u.y; w[4 * k + 2] = u.z; w[4 * k + 3] = u.w;
+      for (int k = 0; k <= HW; ++k) w[k] = 0u;
+      if (valid) {
+        const uint32_t* src = reinterpret_cast<const uint32_t*>(a.v_codes + (row0 + t) * PBV + hh * (PBV / 2));
+        if constexpr (FMTV == 1) {
+#pragma unroll
+          for (int k = 0; k < HW; ++k) w[k] = __ldg(src + k);  // 40-byte halves: 4-byte aligned
+        } else {
+#pragma unroll
+          for (int k = 0; k < HW / 4; ++k) {
+            const uint4 u = __ldg(reinterpret_cast<const uint4*>(src) + k);
+            w[4 * k] = u.x; w[4 * k + 1] = u.y; w[4 * k + 2] = u.z; w[4 * k + 3] = u.w;
+          }
         }
       }
-      w[PBV / 4] = 0u;
-      uint8_t* vrow = vb + (tid >> 3) * 1024 + (tid & 7) * 128;
+      uint8_t* vrow = vb + hh * 16384 + (tok >> 3) * 1024 + (tok & 7) * 128;
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {  // 8 dimensions per 16-byte chunk; chunks 8..15 in the second M block
+      for (int c = 0; c < 8; ++c) {  // 8 dimensions per 16-byte chunk
         uint4 v = make_uint4(0u, 0u, 0u, 0u);
         if (valid) {
-          v.x = at_code_pair<FMTV>(w, 4 * c);
-          v.y = at_code_pair<FMTV>(w, 4 * c + 1);
-          v.z = at_code_pair<FMTV>(w, 4 * c + 2);
-          v.w = at_code_pair<FMTV>(w, 4 * c + 3);
+          const int p0 = 4 * c;  // first dimension pair of the chunk, within this half
+          v.x = at_code_pair<FMTV>(w, p0);
+          v.y = at_code_pair<FMTV>(w, p0 + 1);
+          v.z = at_code_pair<FMTV>(w, p0 + 2);
+          v.w = at_code_pair<FMTV>(w, p0 + 3);
         }
-        *reinterpret_cast<uint4*>(vrow + (c >> 3) * 16384 + (((c & 7) ^ (tid & 7)) << 4)) = v;
+        *reinterpret_cast<uint4*>(vrow + ((c ^ (tok & 7)) << 4)) = v;
       }
     }
-    const float sv = valid ? __half2float(__ushort_as_half(a.v_scales[row0 + t])) : 0.0f;
+    const bool vs = smx && base + tid < t1;  // softmax token tid of the tile
+    const float sv = vs ? __half2float(__ushort_as_half(a.v_scales[row0 + base + tid])) : 0.0f;
     fence_proxy_async_smem();
     tc_fence_before();
     __syncthreads();
@@ -320,31 +395,35 @@ __global__ void __launch_bounds__(kAtTok, 3) attend_partial(const AttendArgs a) 
       }
       umma_commit(&barS);
     }
-    if (!mbar_wait(&barS, ph)) err = 1;
-    tc_fence_after();
-    float x[16];
-    tmem_ld16(tS + lane_off, x);
-    // ---- online softmax over the tile (base-2 logits)
     float s[G];
+    if (smx) {
+      if (!mbar_wait(&barS, ph)) err = 1;
+      tc_fence_after();
+      float x[16];
+      tmem_ld16(tS + lane_off, x);
+      // ---- online softmax over the tile (base-2 logits), thread tid = token tid
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      s[g] = valid ? x[g] * qscale : -INFINITY;
-      float v = s[g];
+      for (int g = 0; g < G; ++g) {
+        s[g] = vs ? x[g] * qscale : -INFINITY;
+        float v = s[g];
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-      if (lane == 0) red[g][warp] = v;
+        for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+        if (lane == 0) red[g][warp] = v;
+      }
     }
     __syncthreads();
     float alpha[G];
+    if (smx) {
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const float tm = fmaxf(fmaxf(red[g][0], red[g][1]), fmaxf(red[g][2], red[g][3]));
-      const float mn = fmaxf(m[g], tm);
-      alpha[g] = m[g] == -INFINITY ? 0.0f : ex2a(m[g] - mn);
-      m[g] = mn;
-      const float p = valid ? ex2a(s[g] - mn) : 0.0f;
-      lsum[g] = fmaf(lsum[g], alpha[g], p);
-      *reinterpret_cast<__half*>(wb + sw128_off(g, tid, 2048)) = __float2half_rn(valid ? p * sv : 0.0f);
+      for (int g = 0; g < G; ++g) {
+        const float tm = fmaxf(fmaxf(red[g][0], red[g][1]), fmaxf(red[g][2], red[g][3]));
+        const float mn = fmaxf(m[g], tm);
+        alpha[g] = m[g] == -INFINITY ? 0.0f : ex2a(m[g] - mn);
+        m[g] = mn;
+        const float p = vs ? ex2a(s[g] - mn) : 0.0f;
+        lsum[g] = fmaf(lsum[g], alpha[g], p);
+        *reinterpret_cast<__half*>(wb + sw128_off(g, tid, 2048)) = __float2half_rn(vs ? p * sv : 0.0f);
+      }
     }
     fence_proxy_async_smem();
     tc_fence_before();
@@ -360,34 +439,40 @@ __global__ void __launch_bounds__(kAtTok, 3) attend_partial(const AttendArgs a) 
       }
       umma_commit(&barO);
     }
-    if (!mbar_wait(&barO, ph)) err = 1;
-    tc_fence_after();
-    float o[16];
-    tmem_ld16(tO + lane_off, o);
+    if (smx) {
+      if (!mbar_wait(&barO, ph)) err = 1;
+      tc_fence_after();
+      float o[16];
+      tmem_ld16(tO + lane_off, o);
 #pragma unroll
-    for (int g = 0; g < G; ++g) acc[g] = fmaf(acc[g], alpha[g], o[g]);
+      for (int g = 0; g < G; ++g) acc[g] = fmaf(acc[g], alpha[g], o[g]);
+    }
     tc_fence_before();
     __syncthreads();  // the tiles and TMEM columns are free for the next tile
     if (err) break;
   }
   // ---- per query head: running max, softmax sum (fixed-order reduction), accumulator
   const int64_t o = ((int64_t)b * a.q_heads + kh * G) * a.splits + split;
+  if (smx) {
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    float v = lsum[g];
+    for (int g = 0; g < G; ++g) {
+      float v = lsum[g];
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-    if (lane == 0) red[g][warp] = v;
+      for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+      if (lane == 0) red[g][warp] = v;
+    }
   }
   __syncthreads();
+  if (smx) {
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    const int64_t og = o + (int64_t)g * a.splits;
-    if (tid == 0) {
-      a.ws_m[og] = m[g];
-      a.ws_l[og] = (red[g][0] + red[g][1]) + (red[g][2] + red[g][3]);
+    for (int g = 0; g < G; ++g) {
+      const int64_t og = o + (int64_t)g * a.splits;
+      if (tid == 0) {
+        a.ws_m[og] = m[g];
+        a.ws_l[og] = (red[g][0] + red[g][1]) + (red[g][2] + red[g][3]);
+      }
+      a.ws_acc[og * kAtD + tid] = acc[g];
     }
-    a.ws_acc[og * kAtD + tid] = acc[g];
   }
   if (tid == 0 && err) {
     // a tile whose MMA was not waited for must finish before TMEM is freed
@@ -479,8 +564,8 @@ int attend_splits(int batch, int heads, int n_tokens) {
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int tiles = (n_tokens + kAtTok - 1) / kAtTok;
-  // one wave of attend_partial at 3 resident CTAs per SM
-  const long long want = (3LL * sms + (long long)batch * heads - 1) / ((long long)batch * heads);
+  // one wave of attend_partial at 2 resident CTAs per SM
+  const long long want = (2LL * sms + (long long)batch * heads - 1) / ((long long)batch * heads);
   return (int)std::max(1LL, std::min<long long>(std::min<long long>(tiles, want), kAtMaxSplits));
 }
 
@@ -490,7 +575,7 @@ static cudaError_t attend_g(const AttendArgs& a, int G, cudaStream_t s) {
   cudaError_t e = cudaSuccess;
   auto run = [&](auto kern) {
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, AtSmem::kBytes);
-    if (e == cudaSuccess) kern<<<grid, kAtTok, AtSmem::kBytes, s>>>(a);
+    if (e == cudaSuccess) kern<<<grid, kAtThreads, AtSmem::kBytes, s>>>(a);
   };
   switch (G) {
     case 1: run(attend_partial<FMTK, FMTV, 1>); break;
