@@ -512,6 +512,11 @@ def entropy_leg(cache, cfg, max_tokens: int = 2048) -> dict:
                  "bits_per_symbol": round(rr["bits_per_symbol"], 4), "stream_bytes": rr["stream_bytes"],
                  "device_seconds": round(rr["device_seconds"], 4), "host_seconds": round(rr["host_seconds"], 4),
                  "host_msymbols_per_s": round(rr["host_msymbols_per_s"], 1)}
+    c = cache.layers[q[0]].codes
+    dev = torch.device("cuda", torch.cuda.current_device())
+    st = E.e8_entropy_stats(c.k_codes[:, :, :min(cache.n_kept, max_tokens)].to(dev), cache.head_dim_padded,
+                            c.key_levels)
+    r["rans"]["shannon_bits_per_symbol_keys"] = round(st["entropy_bps"], 4)  # measure_e8_entropy
     return r
 
 

@@ -21,6 +21,7 @@ from __future__ import annotations
 
 import ctypes
 import ctypes.util
+import math
 import struct
 import time
 import zlib
@@ -391,3 +392,32 @@ def rans_decode_e8(data: bytes):
     sym = rans_decode(words, n_sym, freqs).astype(np.int32)
     codes = (sym - levels) if has_half else 2 * (sym - levels // 2)
     return codes.astype(np.int8), scales
+
+
+def measure_entropy_counts(counts: np.ndarray, alphabet_size: Optional[int] = None) -> Dict[str, float]:
+    """measure_entropy (entropy_coder.py:89-131) from per-symbol counts instead of the symbol
+    stream: Shannon bits per symbol, the uniform code's bits, their ratio, the symbol count and
+    the number of distinct symbols, with the reference's numpy operations in its order."""
+    counts = np.asarray(counts, dtype=np.int64)
+    n = int(counts.sum())
+    if n == 0:
+        return {"entropy_bps": 0, "uniform_bps": 0, "compression_ratio": 1.0, "n_symbols": 0, "n_unique": 0}
+    seen = np.nonzero(counts)[0]            # ascending, as np.unique returns them
+    c = counts[seen]
+    probs = c / n
+    entropy = -np.sum(probs * np.log2(probs + 1e-30))
+    if alphabet_size is None:
+        alphabet_size = int(seen.max()) + 1
+    uniform_bps = math.log2(max(alphabet_size, 2))
+    return {"entropy_bps": float(entropy), "uniform_bps": float(uniform_bps),
+            "compression_ratio": float(uniform_bps / max(entropy, 0.01)), "n_symbols": int(n),
+            "n_unique": int(seen.size)}
+
+
+def e8_entropy_stats(packed: torch.Tensor, head_dim_padded: int, levels: int) -> Dict[str, float]:
+    """measure_e8_entropy (entropy_coder.py:134-159) of packed code rows [..., pb]: the
+    histogram is taken on the device (kernels.code_histogram), the statistics on the host."""
+    cnt = K.code_histogram(packed, head_dim_padded, levels).cpu().numpy().astype(np.int64)
+    has_half = bool(cnt[1::2].sum() > 0)
+    alpha = cnt if has_half else cnt[0::2]
+    return measure_entropy_counts(alpha, alpha.size)

@@ -167,8 +167,8 @@ def rans_case(levels, rows, kind, seed=7):
 
 def make_rans() -> dict:
     """entropy_coder.encode_e8 (entropy_coder.py:405-452) run by the reference on
-    quantized = code / 2 * scale with the row's fp16 scale repeated over its 8-groups, and
-    decode_e8's round trip."""
+    quantized = code / 2 * scale with the row's fp16 scale repeated over its 8-groups,
+    decode_e8's round trip, and measure_e8_entropy's statistics (entropy_coder.py:134-159)."""
     from nexusquant.core import entropy_coder as EC
     fx = {}
     for name, levels, rows, kind in RANS_CASES:
@@ -182,6 +182,9 @@ def make_rans() -> dict:
         fx[f"{name}_levels"] = np.int64(levels)
         fx[f"{name}_stream"] = np.frombuffer(blob, np.uint8)
         fx[f"{name}_roundtrip"] = np.int64(int(torch.equal(dq.reshape(-1, 8).float(), q)))
+        st = EC.measure_e8_entropy(q, torch.from_numpy(sc), levels=levels)
+        fx[f"{name}_entropy"] = np.array([st["entropy_bps"], st["uniform_bps"], st["compression_ratio"],
+                                          st["n_symbols"], st["n_unique"]], np.float64)
     return fx
 
 

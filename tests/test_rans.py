@@ -48,6 +48,18 @@ def test_stream_byte_identical_host(fx, name):
     assert np.array_equal(dc, codes.reshape(-1)) and np.array_equal(ds, np.repeat(s16, codes.shape[1] // 8))
 
 
+@pytest.mark.parametrize("name", NAMES)
+def test_entropy_stats_match_reference(fx, name):
+    """measure_e8_entropy's statistics (the reference's own values) from symbol counts."""
+    codes, levels = fx[f"{name}_codes"], int(fx[f"{name}_levels"])
+    sym, half, a = _symbols(codes, levels)
+    st = E.measure_entropy_counts(np.bincount(sym, minlength=a), a)
+    ref = fx[f"{name}_entropy"]
+    got = np.array([st["entropy_bps"], st["uniform_bps"], st["compression_ratio"], st["n_symbols"],
+                    st["n_unique"]], np.float64)
+    assert np.array_equal(got, ref), (got, ref)
+
+
 def test_freq_table_edge_cases():
     # all counts zero: uniform table with the remainder on symbol 0
     f = E.rans_freq_table(np.zeros(9, np.int64))
@@ -94,6 +106,18 @@ def test_stream_byte_identical_device(fx, orc, name):
     assert np.array_equal(K.code_symbols(packed, 128, levels, half).cpu().numpy().reshape(-1), sym)
     blob = E.rans_encode_e8(packed, torch.from_numpy(s16).cuda(), 128, levels)
     assert blob == bytes(fx[f"{name}_stream"])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", NAMES)
+def test_entropy_stats_device(fx, orc, name):
+    import torch
+    codes, levels = fx[f"{name}_codes"], int(fx[f"{name}_levels"])
+    packed = torch.from_numpy(orc.pack(codes, levels)).cuda()
+    st = E.e8_entropy_stats(packed, 128, levels)
+    ref = fx[f"{name}_entropy"]
+    assert [st["entropy_bps"], st["uniform_bps"], st["compression_ratio"], st["n_symbols"], st["n_unique"]] == \
+        ref.tolist()
 
 
 @pytest.mark.gpu
