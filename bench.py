@@ -552,6 +552,19 @@ def extras_leg(sh, steps: int) -> dict:
         out["attend_compressed"] = {"us": round(us, 2), "kv_heads": hl, "q_heads": 8 * hl, "tokens": sh.cap,
                                     "gbs_of_compressed_bytes": round(nbytes / us / 1e3, 1),
                                     "kernel": "attend_partial (tcgen05 S = K Q^T, O = C^T W^T) + attend_combine"}
+    # the drop-in default layout (fake_quant): codes plus the fp16 reconstruction written back
+    fl = sh.quant[:4]
+    if fl:
+        rk = [torch.empty_like(sh.K[l]) for l in fl]
+        rv = [torch.empty_like(sh.V[l]) for l in fl]
+        kw = dict(key_levels=sh.levels[0], value_levels=sh.levels[1], kept_idx=sh.kept_idx,
+                  kept_count=sh.kept_count, n_kept=sh.cap, rope_base=cfg.rope_base, rope_rows=cfg.seq)
+        ms_c = timed(lambda: K.compress_layers([sh.K[l] for l in fl], [sh.V[l] for l in fl], **kw), 5, 3, 1) / 5
+        ms_r = timed(lambda: K.compress_layers([sh.K[l] for l in fl], [sh.V[l] for l in fl], recon_k=rk, recon_v=rv,
+                                               **kw), 5, 3, 1) / 5
+        out["compress_fake_quant"] = {"layers": len(fl), "ms_codes": round(ms_c, 4),
+                                      "ms_codes_plus_fp16_reconstruction": round(ms_r, 4)}
+        del rk, rv
     layers = sh.quant[:8]
     if cfg.eviction_rate > 0 and len(layers) == 8 and cfg.head_dim == 128 and cfg.batch == 1:
         cen = sum(sh.V[l][0].float().mean(0) for l in layers) / 8.0

@@ -570,7 +570,91 @@ __device__ __forceinline__ void compress_tile(const CompressArgs& a, const Tile&
     float* sc32 = KEY ? L.k_scales_f32 : L.v_scales_f32;
     if (sc32) sc32[vrow] = sc;
   }
-  if constexpr (RECON) {
+  if constexpr (RECON && D == DP) {
+    // Fake-quant reconstruction, split like the forward path: this thread rebuilds its own
+    // pairs {x[q], x[q + DP/2]} (q in [h HP, (h + 1) HP)) from its groups' codes; the inverse
+    // butterfly runs on exact integers (|partial sums| <= 16 DP), so its order does not change
+    // a bit; then * fl(sc / 2 * h), forward RoPE at the output position, sharpening and fp16,
+    // each rounded as recon_store rounds them.
+    uint16_t* out = KEY ? L.k_out : L.v_out;
+    if (out) {
+      u64 R[HP];
+#pragma unroll
+      for (int g = 0; g < GT; ++g)
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          R[8 * g + i] = pk(static_cast<float>(group_code<FMT>(gl_all[g], i)),
+                            static_cast<float>(group_code<FMT>(gh_all[g], i)));
+      if (a.rotate) {
+#pragma unroll
+        for (int st = 1; st < HP; st <<= 1) {
+#pragma unroll
+          for (int q = 0; q < HP; ++q) {
+            if ((q & st) == 0) {
+              const u64 u = R[q], w2 = R[q + st];
+              R[q] = add2(u, w2);
+              R[q + st] = sub2(u, w2);
+            }
+          }
+        }
+        const float sg = h ? -1.0f : 1.0f;
+        const u64 sg2 = pk(sg, sg);
+#pragma unroll
+        for (int q = 0; q < HP; ++q) {
+          const u64 o = __shfl_xor_sync(0xffffffffu, R[q], 1);
+          R[q] = fma2(R[q], sg2, o);
+        }
+#pragma unroll
+        for (int q = 0; q < HP; ++q) {
+          float u, w2;
+          upk(R[q], u, w2);
+          R[q] = pk(__fadd_rn(u, w2), __fsub_rn(u, w2));
+        }
+      }
+      if (valid) {
+        const int src_row = a.kept_idx ? a.kept_idx[(int64_t)t.b * a.n_kept + j] : j;
+        const int pos = min(max(a.positions ? a.positions[(int64_t)t.b * a.n_kept + j] : src_row, 0), a.rope_rows - 1);
+        const int orow = a.out_row_mode == 1 ? j : src_row;
+        int opos = pos;
+        if (a.out_positions) opos = a.out_positions[(int64_t)t.b * a.n_kept + j];
+        else if (a.out_row_mode == 1) opos = j;
+        opos = min(max(opos, 0), a.rope_rows - 1);
+        __half* o = reinterpret_cast<__half*>(out) + (int64_t)t.b * a.out_stride_b +
+                    (int64_t)head * a.out_stride_h + (int64_t)orow * a.out_stride_t;
+        const float coef = __fmul_rn(sc, a.rotate ? 0.5f * hadamard_entry(DP) : 0.5f);
+        const u64 coef2 = pk(coef, coef), sh2 = pk(a.key_sharpen, a.key_sharpen);
+        const float* cr = a.rope_cos + (int64_t)opos * (D / 2) + q0;
+        const float* sr = a.rope_sin + (int64_t)opos * (D / 2) + q0;
+#pragma unroll
+        for (int k = 0; k < HP / 8; ++k) {
+          uint32_t lo[4], hi[4];
+#pragma unroll
+          for (int u = 0; u < 8; u += 2) {
+            float y1[2], y2[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int q = 8 * k + u + e;
+              u64 z = mul2(R[q], coef2);
+              if constexpr (KEY) {
+                const float c = __ldg(cr + q), sn2 = __ldg(sr + q);
+                float m1, m2, n1, n2;
+                upk(mul2(z, pk(c, c)), m1, m2);
+                upk(mul2(z, pk(sn2, sn2)), n1, n2);
+                z = pk(__fsub_rn(m1, n2), __fadd_rn(n1, m2));
+                if (a.key_sharpen != 1.0f) z = mul2(z, sh2);
+              }
+              upk(z, y1[e], y2[e]);
+            }
+            const __half2 hl = __floats2half2_rn(y1[0], y1[1]), hv = __floats2half2_rn(y2[0], y2[1]);
+            lo[u / 2] = *reinterpret_cast<const uint32_t*>(&hl);
+            hi[u / 2] = *reinterpret_cast<const uint32_t*>(&hv);
+          }
+          reinterpret_cast<uint4*>(o + q0)[k] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+          reinterpret_cast<uint4*>(o + H2 + q0)[k] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        }
+      }
+    }
+  } else if constexpr (RECON) {
     uint16_t* out = KEY ? L.k_out : L.v_out;
     if (out) {
       // assemble the full code vector in the lower thread of the pair

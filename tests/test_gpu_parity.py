@@ -455,3 +455,42 @@ def test_positions_past_the_rope_table_are_clamped():
     want = K.attend_compressed(q, lc, far.clamp(max=rows - 1), rope_base=base, rope_rows=rows)
     torch.cuda.synchronize()
     assert torch.equal(got, want)
+
+
+@pytest.mark.parametrize("d,kl,vl,sharpen,rows", [(128, 4, 4, 1.0, "source"), (128, 8, 4, K.SHARPEN, "kept"),
+                                                   (64, 4, 16, 1.0, "kept"), (64, 8, 8, K.SHARPEN, "source")])
+def test_fake_quant_recon_kept_rows(orc, d, kl, vl, sharpen, rows):
+    """Fake-quant reconstruction of fp16 layers through a keep set (each thread of a vector's
+    pair rebuilds its own half): bit-exact against the oracle's dequantize with the fp32
+    scales, keys re-encoded at the source position (masked layout) or at the kept index j
+    (truncated layout), sharpened or not."""
+    b, h, T = 2, 3, 700
+    g = torch.Generator().manual_seed(17 + d + kl)
+    k = (torch.randn(b, h, T, d, generator=g)).half()
+    v = (torch.randn(b, h, T, d, generator=g)).half()
+    n = 300
+    kept = np.stack([np.sort(np.random.default_rng(bi).choice(T, n, replace=False)) for bi in range(b)])
+    kidx = torch.as_tensor(kept, dtype=torch.int32, device=DEV)
+    cnt = torch.full((b,), n, dtype=torch.int32, device=DEV)
+    shape_o = (b, h, T if rows == "source" else n, d)
+    ok = torch.zeros(shape_o, dtype=torch.float16, device=DEV)
+    ov = torch.zeros(shape_o, dtype=torch.float16, device=DEV)
+    lc = K.compress_layers([k.to(DEV)], [v.to(DEV)], key_levels=kl, value_levels=vl, kept_idx=kidx, kept_count=cnt,
+                           n_kept=n, recon_k=[ok], recon_v=[ov], recon_rows=rows, key_sharpen=sharpen,
+                           emit_scales_f32=True, rope_rows=T)[0]
+    okh, ovh = ok.cpu().numpy(), ov.cpu().numpy()
+    for bi in range(b):
+        kr = k[bi][:, kept[bi]].float().numpy().reshape(-1, d)
+        vr = v[bi][:, kept[bi]].float().numpy().reshape(-1, d)
+        c_in, s_in = orc.rope_tables(kept[bi], d, 10000.0)
+        kc, _ = orc.quantize(kr, d, kl, np.tile(c_in, (h, 1)), np.tile(s_in, (h, 1)))
+        vc, _ = orc.quantize(vr, d, vl)
+        ks32 = lc.k_scales_f32[bi].cpu().numpy().reshape(-1)
+        vs32 = lc.v_scales_f32[bi].cpu().numpy().reshape(-1)
+        opos = kept[bi] if rows == "source" else np.arange(n)
+        c_out, s_out = orc.rope_tables(opos, d, 10000.0)
+        kx = orc.dequantize(kc, ks32, d, np.tile(c_out, (h, 1)), np.tile(s_out, (h, 1)), sharpen=sharpen)
+        vx = orc.dequantize(vc, vs32, d).astype(np.float16)
+        sel = kept[bi] if rows == "source" else np.arange(n)
+        assert np.array_equal(okh[bi][:, sel].reshape(-1, d), kx.astype(np.float16))
+        assert np.array_equal(ovh[bi][:, sel].reshape(-1, d), vx)
