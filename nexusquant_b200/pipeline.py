@@ -230,6 +230,12 @@ def _compress_to_host(keys, values, quant, prot, klv, vlv, kept_idx, kept_count,
                     pv_ = prev.v_fp16 if prev is not None and prev.protected else None
                     layers[i] = CompressedLayer(k_fp16=to_host(kf, pk_), v_fp16=to_host(vf, pv_))
 
+    # protected layers first: their fp16 rows are the largest copies back, and issued first
+    # they travel while the quantized groups are gathered and compressed
+    for i in prot:
+        kf = K.gather_rows(keys[i], kept_idx, n_kept, kept_count, device=dev if host_in else None)
+        vf = K.gather_rows(values[i], kept_idx, n_kept, kept_count, device=dev if host_in else None)
+        flush([i], {i: (kf, vf)})
     groups = [quant[i:i + group_layers] for i in range(0, len(quant), max(1, group_layers))]
     for grp in groups:
         for sub in _group_layers(keys, grp):
@@ -239,10 +245,6 @@ def _compress_to_host(keys, values, quant, prot, klv, vlv, kept_idx, kept_count,
                                       rope_base=rope_base, rope_scaling=rope_scaling,
                                       device=dev if host_in else None)
             flush(sub, dict(zip(sub, codes)))
-    for i in prot:
-        kf = K.gather_rows(keys[i], kept_idx, n_kept, kept_count, device=dev if host_in else None)
-        vf = K.gather_rows(values[i], kept_idx, n_kept, kept_count, device=dev if host_in else None)
-        flush([i], {i: (kf, vf)})
     done = torch.cuda.Event()
     done.record(cp)
     comp.wait_event(done)  # the caller's stream (and a synchronize on it) covers the copies
