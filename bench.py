@@ -77,7 +77,8 @@ def config_dict(cfg, cap: int, world: int) -> dict:
             "seq": cfg.seq, "head_dim": cfg.head_dim, "key_bits": cfg.key_bits, "value_bits": cfg.value_bits,
             "eviction_rate": cfg.eviction_rate, "scorer": cfg.scorer if cfg.eviction_rate > 0 else "none",
             "kept_tokens": cap, "protected_layers": sorted(S.protected_layers(cfg.n_layers, cfg.protect_boundary)),
-            "parallelism": f"head-sharded x{world}" if cfg.heads % world == 0 else f"layer-sharded x{world}",
+            "parallelism": (f"head-sharded x{world}" if S.plan_mode(cfg.heads, world) == "heads"
+                            else f"layer-sharded x{world}"),
             "l2": f"inputs ({cfg.fp16_bytes / 1e9:.2f} GB) larger than L2; no flush"}
 
 

@@ -3,11 +3,17 @@
 Once the keep set is known every (layer, KV head) row block compresses
 independently.  Two plans:
 
-* ``heads`` (when the world size divides the KV heads): rank r owns KV heads
-  [r*h/N, (r+1)*h/N) of every layer -- the same slice it scores -- so every rank
-  moves exactly 1/N of the cache, protected layers included.
+* ``heads`` (when the world size divides the KV heads and leaves every rank at
+  least ``MIN_HEADS_PER_RANK`` of them): rank r owns KV heads [r*h/N, (r+1)*h/N)
+  of every layer -- the same slice it scores -- so every rank moves exactly 1/N of
+  the cache, protected layers included.
 * ``layers`` (otherwise): ranks own whole layers, balanced by cost
-  (longest-processing-time greedy).
+  (longest-processing-time greedy).  A compress tile covers up to 8 heads of one
+  token, which share that token's RoPE row; with fewer heads per layer on a rank
+  the key tiles read one RoPE row per vector and the kernel slows down (config 4
+  at 8 ranks: 0.23 of the HBM peak with one head per rank against 0.33 with all
+  eight), which costs more than the whole-layer plan's imbalance (10 against an
+  even 9.5 quantized layers per rank at 8 ranks).
 
 The only cross-GPU traffic:
 
@@ -95,9 +101,16 @@ class ShardPlan:
         return (self.head_begin, self.head_end) if self.mode == "heads" else (0, self.heads)
 
 
+# Fewest KV heads per layer a rank keeps under the ``heads`` plan chosen by ``mode="auto"``:
+# the compress kernel's tiles group up to 8 heads of a token around one RoPE row.
+MIN_HEADS_PER_RANK = 8
+
+
 def plan_mode(heads: int, world: int, mode: str = "auto") -> str:
     if mode == "auto":
-        return "heads" if heads % world == 0 else "layers"
+        if world == 1:
+            return "heads"
+        return "heads" if heads % world == 0 and heads // world >= MIN_HEADS_PER_RANK else "layers"
     if mode not in ("heads", "layers"):
         raise ValueError(f"mode must be 'auto', 'heads' or 'layers', got {mode!r}")
     if mode == "heads" and heads % world:
@@ -217,16 +230,24 @@ def step_checkpoint(store, rank: int, world: int, step: int, timeout: float = 30
     collective of the next step is launched -- the survivors raise RankFailure instead of
     blocking in NCCL.  ``store`` is the process group's store (or any c10d Store)."""
     key = "nq/step/{}/{}".format
-    store.set(key(step, rank), b"1")
     deadline = time.monotonic() + timeout
     missing = [r for r in range(world) if r != rank]
-    while missing:
-        missing = [r for r in missing if not store.check([key(step, r)])]
-        if not missing:
-            return
-        if time.monotonic() > deadline:
-            raise RankFailure(f"rank(s) {missing} did not reach step {step} within {timeout:g} s")
-        time.sleep(0.005)
+    try:
+        store.set(key(step, rank), b"1")
+        while missing:
+            missing = [r for r in missing if not store.check([key(step, r)])]
+            if not missing:
+                return
+            if time.monotonic() > deadline:
+                raise RankFailure(f"rank(s) {missing} did not reach step {step} within {timeout:g} s")
+            time.sleep(0.005)
+    except RankFailure:
+        raise
+    except RuntimeError as e:
+        # the store itself went away: the rank hosting it (rank 0 for a TCPStore) has left,
+        # which is a peer failure like any other
+        raise RankFailure(f"rank(s) {missing} did not reach step {step}: store unreachable "
+                          f"({type(e).__name__})") from e
 
 
 def validate_index(sizes_all: torch.Tensor, n_layers: int, heads: int, protect_boundary: int,

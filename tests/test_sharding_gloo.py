@@ -138,12 +138,30 @@ def test_head_blocks_cover_heads(heads, world):
 
 @pytest.mark.parametrize("world", [1, 2, 4, 8])
 def test_head_plan_config4_is_even(world):
-    """Config 4 (80 layers, 8 KV heads): every rank compresses 8/world heads of all 76 quantized
-    layers and gathers the same slice of the 4 protected ones."""
-    plans = [S.make_plan(80, 8, 2, r, world) for r in range(world)]
+    """Config 4 (80 layers, 8 KV heads) under mode="heads": every rank compresses 8/world heads
+    of all 76 quantized layers and gathers the same slice of the 4 protected ones."""
+    plans = [S.make_plan(80, 8, 2, r, world, mode="heads") for r in range(world)]
     assert all(p.mode == "heads" for p in plans)
     assert [p.layer_heads for p in plans] == [(r * 8 // world, (r + 1) * 8 // world) for r in range(world)]
     assert all(len(p.quantized) == 76 and len(p.protected) == 4 for p in plans)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_auto_plan_config4_keeps_whole_layers(world):
+    """mode="auto" on config 4: 8 KV heads split over 2-8 ranks would leave fewer than
+    MIN_HEADS_PER_RANK per rank, so ranks own whole layers; the scored head blocks still
+    cover every head once and the quantized layers are as even as whole layers allow."""
+    plans = [S.make_plan(80, 8, 2, r, world) for r in range(world)]
+    assert all(p.mode == "layers" and p.layer_heads == (0, 8) for p in plans)
+    assert sorted(l for p in plans for l in p.layers) == list(range(80))
+    assert max(len(p.quantized) for p in plans) == -(-76 // world)
+    assert [h for p in plans for h in range(p.head_begin, p.head_end)] == list(range(8))
+
+
+def test_auto_plan_heads_when_every_rank_keeps_enough():
+    assert S.make_plan(32, 32, 2, 0, 4).mode == "heads"   # 8 heads per rank
+    assert S.make_plan(32, 32, 2, 0, 8).mode == "layers"  # 4 heads per rank
+    assert S.make_plan(80, 8, 2, 0, 1).mode == "heads"    # one rank: the whole cache
 
 
 def test_plan_modes():
