@@ -12,10 +12,11 @@ runs the real-attention scorer over every layer's 64 synthetic queries instead.
 
 One step = score (each rank scores its block of KV heads; per-head column sums are
 all-gathered over NCCL, or for the real scorer the per-rank sums are all-reduced) ->
-keep set -> compress every (layer, head slice) the rank owns (one launch per half) +
+keep set -> compress every layer (or head slice) the rank owns (one launch per half) +
 fp16 gather of its share of the protected layers -> all-gather of the per-layer
-compressed sizes.  With N dividing the KV heads each rank owns N-th of the heads of every
-layer (strong scaling: the cache is fixed, N GPUs share it).  value = fp16-in bytes of the
+compressed sizes.  Ranks own whole layers (sharding.make_plan, mode "auto"; head slices only
+when every rank would keep 8 or more KV heads).  Strong scaling: the cache is fixed, N GPUs
+share it.  value = fp16-in bytes of the
 whole cache / max-over-ranks step time.  Inputs are far larger than L2, so no flush is
 needed between steps.
 
@@ -214,7 +215,7 @@ class Shard:
         self.nk = n_keep_for(cfg.seq, cfg.sliding_window, cfg.eviction_rate)
         self.cap = cap_for(cfg)
         b, T, d = cfg.batch, cfg.seq, cfg.head_dim
-        # resident data: this rank's head slice of its layers
+        # resident data: this rank's layers (its head slice of them under the head plan)
         self.K, self.V, self.Q = {}, {}, {}
         for l in self.owned:
             k, v = syn.device_layer(cfg, l, device)
