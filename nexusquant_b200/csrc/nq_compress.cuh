@@ -384,6 +384,26 @@ __device__ __forceinline__ void issue_tile(const CompressArgs& a, const Tile& t,
   }
 }
 
+// Coordinates j0 .. j0+7 of a staged row (j0 a multiple of 8), widened to fp32 and, for keys,
+// inverse-rotated at the row's position: y_i = x_i c + x_{i+HF} s, y_{i+HF} = x_{i+HF} c - x_i s,
+// each rounded as the whole-row rotation rounds it.
+template <typename TIn, bool KEY, int HF>
+__device__ __forceinline__ void chunk_in(const TIn* r, const float* cs, const float* sn, int j0, float (&x)[8]) {
+  load8(r + j0, x);
+  if constexpr (KEY) {
+    const bool up = j0 < HF;
+    const int i0 = up ? j0 : j0 - HF;
+    float pr[8];
+    load8(r + (up ? j0 + HF : i0), pr);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const float c = cs[i0 + u], s = sn[i0 + u];
+      const float a = __fmul_rn(x[u], c), b = __fmul_rn(pr[u], s);
+      x[u] = up ? __fadd_rn(a, b) : __fsub_rn(a, b);
+    }
+  }
+}
+
 // --------------------------------------------------------------------------
 // Per-vector body (two threads per vector), one tile of K or V, one format.
 // Thread h of the pair owns pairs P[q] = {x[q], x[q + DP/2]} for q in
@@ -440,26 +460,22 @@ __device__ __forceinline__ void compress_tile(const CompressArgs& a, const Tile&
       }
     }
   } else {
-    // D < DP (96 -> 128): RoPE pairs (i, i + D/2) straddle the two threads, so each
-    // thread rotates the whole row and keeps its own coordinates.
-    float x[D];
+    // D < DP (96 -> 128): thread h needs coordinates j = h*HP + q (low) and H2 + h*HP + q
+    // (high; past D they are the zero pad).  Chunks of 8 coordinates never straddle D/2 or D,
+    // so each thread loads (and, for keys, inverse-rotates) only the chunks it owns: the chunk
+    // addresses differ between the two threads of a pair, the code does not.
+    constexpr int HF = D / 2;
+    static_assert(HF % 8 == 0 && (D - H2) % 8 == 0 && D >= H2 && HP % 8 == 0, "chunking of the padded path");
 #pragma unroll
-    for (int k = 0; k < D / 8; ++k) load8(r + 8 * k, &x[8 * k]);
-    if constexpr (KEY) {
+    for (int k = 0; k < HP / 8; ++k) {
+      const int jl = h * HP + 8 * k;
+      const int jh0 = H2 + h * HP + 8 * k;
+      const bool vh = jh0 < D;
+      float lo[8], hi[8];
+      chunk_in<TIn, KEY, HF>(r, cs, sn, jl, lo);
+      chunk_in<TIn, KEY, HF>(r, cs, sn, vh ? jh0 : jl, hi);  // a valid chunk; replaced by the pad
 #pragma unroll
-      for (int i = 0; i < D / 2; ++i) {
-        const float c = cs[i], s = sn[i];
-        const float x1 = x[i], x2 = x[i + D / 2];
-        x[i] = __fadd_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
-        x[i + D / 2] = __fsub_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
-      }
-    }
-#pragma unroll
-    for (int q = 0; q < HP; ++q) {
-      const float lo0 = x[q], lo1 = x[q + HP];
-      const float hi0 = q + H2 < D ? x[q + H2] : 0.0f;
-      const float hi1 = q + HP + H2 < D ? x[q + HP + H2] : 0.0f;
-      P[q] = h ? pk(lo1, hi1) : pk(lo0, hi0);
+      for (int i = 0; i < 8; ++i) P[8 * k + i] = pk(lo[i], vh ? hi[i] : 0.0f);
     }
   }
 
